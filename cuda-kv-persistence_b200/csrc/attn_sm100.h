@@ -1,0 +1,49 @@
+// BF16 tcgen05 remapped attention (csrc/attn_sm100.cu): descriptors and launcher.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace kvp {
+
+// Bits of the device status word (kvp_read_status).
+constexpr int KVP_STATUS_MAP = 1;      // a KVMap entry pointed outside the arena (base row read)
+constexpr int KVP_STATUS_TIMEOUT = 2;  // a bounded wait expired; the CTA's output is incomplete
+
+// One layer's buffers.  Q/K/V/Out are bf16 [rows][D] (head h at columns
+// [h*128, h*128+128)); the arena is bf16 [arena_rows][2*D] (K half, V half);
+// kvmap (int64, may be null) is indexed by the absolute key row.
+struct LayerIO {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* out;
+    const void* arena;
+    const long long* kvmap;
+    long long q_rows, kv_rows, arena_rows;
+};
+
+// Which query rows attend to which key rows.
+//   query frames [q_frame0, q_frame0 + frames) of `tokens` rows each;
+//   mode 0 (intra): frame f's keys are rows [f*T, (f+1)*T);
+//   mode 1 (causal): frame f's keys are rows [b*T, (f+1)*T) with
+//        b = window ? max(0, f-window+1) : 0;
+//   flat = 1 (causal, no window): 128-row query tiles run across frame
+//        boundaries, each row masked at its own frame's limit (no padding
+//        work at the 1560 = 12*128 + 24 frame tail).
+struct AttnDesc {
+    int tokens;
+    int frames;
+    int q_frame0;
+    int mode;
+    int window;
+    int heads;
+    int head_dim;   // must be 128
+    int head0;
+    int nheads;
+    int flat;
+};
+
+int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream);
+
+}  // namespace kvp

@@ -1,0 +1,424 @@
+// extern "C" boundary of libkvp.so.  Declarations and the reference
+// interface each export replaces are in include/kv_tile_manager.h,
+// include/attn_kernel.h and include/kvp.h.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "kernels.h"
+#include "kv_tile_manager.h"
+#include "kvp_common.h"
+#include "session.h"
+#include "tile_gating_policy.h"
+#include "tile_layout.h"
+
+namespace kvp {
+
+namespace {
+thread_local char g_err[512] = "";
+
+// One device status word per device, allocated on first use.
+int* status_word() {
+    static int* words[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!words[dev]) {
+        int* p = nullptr;
+        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
+        words[dev] = p;
+    }
+    return words[dev];
+}
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+}
+
+const char* last_error() { return g_err; }
+
+int cuda_status(cudaError_t e, const char* what) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return KVP_ERR_CUDA;
+}
+
+}  // namespace kvp
+
+using kvp::KVTileManager;
+
+// ===================================================================== kvtm_*
+// Reference facade: src/kv_tile_manager.cu:223-339 (same names, argument
+// meaning and return codes).
+
+KVP_API void* kvtm_create(long budget_bytes, long max_window_bytes) {
+    try {
+        return new KVTileManager((size_t)budget_bytes, (size_t)max_window_bytes);
+    } catch (...) {
+        return nullptr;
+    }
+}
+KVP_API void kvtm_destroy(void* m) { delete static_cast<KVTileManager*>(m); }
+KVP_API int kvtm_init(void* m) { return static_cast<KVTileManager*>(m)->init() ? 1 : 0; }
+KVP_API long kvtm_query_limit(void* m) {
+    return (long)static_cast<KVTileManager*>(m)->query_device_limit();
+}
+KVP_API int kvtm_admit(void* m, long tile_id, void* ptr, long bytes) {
+    return (int)static_cast<KVTileManager*>(m)->admit(tile_id, ptr, (size_t)bytes);
+}
+KVP_API int kvtm_release(void* m, long tile_id) {
+    return static_cast<KVTileManager*>(m)->release(tile_id) ? 1 : 0;
+}
+KVP_API void kvtm_clear(void* m) { static_cast<KVTileManager*>(m)->clear(); }
+KVP_API long kvtm_persisted_bytes(void* m) {
+    return (long)static_cast<KVTileManager*>(m)->persisted_bytes();
+}
+KVP_API int kvtm_persisted_tiles(void* m) {
+    return static_cast<KVTileManager*>(m)->persisted_tiles();
+}
+KVP_API void* kvtm_dev_alloc(long bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return nullptr;
+    return p;
+}
+KVP_API void kvtm_dev_free(void* p) { cudaFree(p); }
+
+KVP_API int kvtm_arena_init(void* m, long cap_bytes, long row_stride_floats) {
+    return static_cast<KVTileManager*>(m)->arena_init((size_t)cap_bytes, (size_t)row_stride_floats)
+               ? 1 : 0;
+}
+KVP_API void kvtm_arena_begin(void* m) { static_cast<KVTileManager*>(m)->arena_begin_step(); }
+KVP_API int kvtm_arena_stage(void* m, const void* k_dev, long k_bytes, const void* v_dev,
+                             long v_bytes, long* out_row) {
+    return static_cast<KVTileManager*>(m)->arena_stage(k_dev, (size_t)k_bytes, v_dev,
+                                                       (size_t)v_bytes, out_row) ? 1 : 0;
+}
+KVP_API int kvtm_arena_window(void* m) {
+    return static_cast<KVTileManager*>(m)->arena_apply_window() ? 1 : 0;
+}
+KVP_API void kvtm_arena_end(void* m) { static_cast<KVTileManager*>(m)->arena_end_step(); }
+KVP_API long kvtm_arena_used(void* m) {
+    return (long)static_cast<KVTileManager*>(m)->arena_used_bytes();
+}
+KVP_API void* kvtm_arena_ptr(void* m) { return static_cast<KVTileManager*>(m)->arena_device_ptr(); }
+
+KVP_API int kvtm_streaming_begin(void* m) {
+    return static_cast<KVTileManager*>(m)->streaming_begin() ? 1 : 0;
+}
+KVP_API int kvtm_streaming_stage(void* m, long row_id, const void* k_dev, long k_bytes,
+                                 const void* v_dev, long v_bytes, int changed, long* out_slot,
+                                 int* restaged) {
+    bool r = false;
+    long slot = -1;
+    const int ok = static_cast<KVTileManager*>(m)->streaming_stage(
+        row_id, k_dev, (size_t)k_bytes, v_dev, (size_t)v_bytes, changed != 0, &slot, &r);
+    if (out_slot) *out_slot = slot;
+    if (restaged) *restaged = r ? 1 : 0;
+    return ok;
+}
+KVP_API int kvtm_streaming_release(void* m, long row_id) {
+    return static_cast<KVTileManager*>(m)->streaming_release(row_id) ? 1 : 0;
+}
+KVP_API int kvtm_streaming_window(void* m) {
+    return static_cast<KVTileManager*>(m)->streaming_apply_window() ? 1 : 0;
+}
+KVP_API void kvtm_streaming_end(void* m) { static_cast<KVTileManager*>(m)->streaming_end(); }
+KVP_API long kvtm_streaming_staged_bytes(void* m) {
+    return (long)static_cast<KVTileManager*>(m)->streaming_staged_bytes();
+}
+
+KVP_API long kvtm_layout_tiles_per_frame(int tokens_per_frame, int tile_tokens) {
+    return kvp::TileLayout(tokens_per_frame, tile_tokens).tiles_per_frame;
+}
+KVP_API long kvtm_layout_tile_start(int tpf, int tt, long id) {
+    return kvp::TileLayout(tpf, tt).tile_start(id);
+}
+KVP_API int kvtm_layout_tile_count(int tpf, int tt, long id) {
+    return kvp::TileLayout(tpf, tt).tile_count(id);
+}
+
+// --- kvtm_* additions (no counterpart in the reference facade)
+KVP_API void* kvtm_create_ex(long budget_bytes, long max_window_bytes, unsigned flags) {
+    try {
+        return new KVTileManager((size_t)budget_bytes, (size_t)max_window_bytes, flags);
+    } catch (...) {
+        return nullptr;
+    }
+}
+KVP_API void kvtm_set_stream(void* m, void* stream) {
+    static_cast<KVTileManager*>(m)->set_stream((cudaStream_t)stream);
+}
+KVP_API int kvtm_flush(void* m) { return static_cast<KVTileManager*>(m)->flush(); }
+KVP_API long kvtm_pending_copies(void* m) {
+    return (long)static_cast<KVTileManager*>(m)->pending_copies();
+}
+KVP_API long kvtm_window_log(void* m, long* bytes_out, int* prop_out, long cap) {
+    const auto& log = static_cast<KVTileManager*>(m)->window_log();
+    const long n = (long)log.size();
+    for (long i = 0; i < n && i < cap; ++i) {
+        if (bytes_out) bytes_out[i] = (long)log[(size_t)i].bytes;
+        if (prop_out) prop_out[i] = log[(size_t)i].hit_prop;
+    }
+    return n;
+}
+KVP_API long kvtm_reset_calls(void* m) { return static_cast<KVTileManager*>(m)->reset_calls(); }
+
+// ============================================================ attn_forward_*
+// Reference entry points src/attn_kernel.h:15-29 (C linkage here).
+
+KVP_API void attn_forward_launcher(const float* d_q, const float* d_k, const float* d_v,
+                                   const float* d_arena, const long* d_kvmap, float* d_out,
+                                   int frames, int T, int D, int heads, bool remap) {
+    kvp::flush_all_managers();
+    int* st = kvp::status_word();
+    if (remap) {
+        // Per-frame intra launches with per-frame map slices (legacy path).
+        for (int f = 0; f < frames; ++f)
+            kvp::launch_attn_fp32(d_q + (size_t)f * T * D, d_k + (size_t)f * T * D,
+                                  d_v + (size_t)f * T * D, d_arena,
+                                  d_kvmap ? (const int64_t*)d_kvmap + (size_t)f * T : nullptr,
+                                  d_out + (size_t)f * T * D, T, D, heads, 0, T, INT64_MAX, 1, 0,
+                                  st, 0);
+    } else {
+        kvp::launch_attn_fp32(d_q, d_k, d_v, nullptr, nullptr, d_out, T, D, heads, 0, T, 0,
+                              frames, T, st, 0);
+    }
+}
+
+KVP_API void attn_forward_single_frame(const float* d_q_f, const float* d_k, const float* d_v,
+                                       const float* d_arena, const long* d_kvmap_f,
+                                       float* d_out_f, int T, int D, int heads, int cross,
+                                       int frame_idx) {
+    kvp::flush_all_managers();
+    const int64_t span = cross ? (int64_t)(frame_idx + 1) * T : (int64_t)T;
+    kvp::launch_attn_fp32(d_q_f, d_k, d_v, d_arena, (const int64_t*)d_kvmap_f, d_out_f, T, D,
+                          heads, 0, span, INT64_MAX, 1, 0, kvp::status_word(), 0);
+}
+
+// ===================================================================== kvp_*
+
+KVP_API const char* kvp_version(void) { return "kvp-b200 1.0 (sm_100a)"; }
+KVP_API const char* kvp_last_error(void) { return kvp::last_error(); }
+
+// Status word the kernels set on a recoverable device error (1 = KVMap entry
+// outside the arena).  Reading it clears it.
+KVP_API int kvp_read_status(void* stream) {
+    int* w = kvp::status_word();
+    if (!w) return kvp::KVP_ERR_CUDA;
+    int h = 0;
+    if (cudaMemcpyAsync(&h, w, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream) != cudaSuccess)
+        return kvp::KVP_ERR_CUDA;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return kvp::KVP_ERR_CUDA;
+    if (h && cudaMemsetAsync(w, 0, sizeof(int), (cudaStream_t)stream) != cudaSuccess)
+        return kvp::KVP_ERR_CUDA;
+    return h;
+}
+
+struct kvp_device_info {
+    int device;
+    int sm_count;
+    int cc_major, cc_minor;
+    long long l2_bytes;
+    long long max_persisting_l2_bytes;
+    long long max_access_policy_window_bytes;
+    long long persisting_limit_bytes;
+    long long hbm_bytes;
+};
+
+KVP_API int kvp_query_device(int device, kvp_device_info* out) {
+    if (!out) return kvp::KVP_ERR_ARG;
+    std::memset(out, 0, sizeof *out);
+    int dev = device;
+    if (dev < 0) KVP_CUDA(cudaGetDevice(&dev));
+    out->device = dev;
+    int v = 0;
+    KVP_CUDA(cudaDeviceGetAttribute(&out->sm_count, cudaDevAttrMultiProcessorCount, dev));
+    KVP_CUDA(cudaDeviceGetAttribute(&out->cc_major, cudaDevAttrComputeCapabilityMajor, dev));
+    KVP_CUDA(cudaDeviceGetAttribute(&out->cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
+    KVP_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrL2CacheSize, dev));
+    out->l2_bytes = v;
+    KVP_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMaxPersistingL2CacheSize, dev));
+    out->max_persisting_l2_bytes = v;
+    KVP_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMaxAccessPolicyWindowSize, dev));
+    out->max_access_policy_window_bytes = v;
+    size_t lim = 0;
+    int cur = -1;
+    KVP_CUDA(cudaGetDevice(&cur));
+    if (cur == dev) {
+        KVP_CUDA(cudaDeviceGetLimit(&lim, cudaLimitPersistingL2CacheSize));
+        out->persisting_limit_bytes = (long long)lim;
+    }
+    size_t free_b = 0, total_b = 0;
+    if (cur == dev && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) out->hbm_bytes = (long long)total_b;
+    return kvp::KVP_OK;
+}
+
+// Policy selection through the C ABI: the reference's
+// TileGatingPolicy::select (src/tile_gating_policy.h:14-15) by policy id
+// (0 none, 1 uniform, 2 recency, 3 motion, 4 reuse_weighted).
+KVP_API int tgp_select(int policy, const float* scores, int n, int max_tiles, int tiles_per_frame,
+                       int total_frames, long* out_ids, int* out_count) {
+    if (!out_count || (!out_ids && max_tiles > 0) || (!scores && n > 0 && policy >= 3))
+        return kvp::KVP_ERR_ARG;
+    kvp::TileGatingPolicy* p = kvp::make_policy(policy, tiles_per_frame > 0 ? tiles_per_frame : 1,
+                                                total_frames);
+    if (!p) return kvp::KVP_ERR_ARG;
+    p->select(scores, n, max_tiles, out_ids, out_count);
+    delete p;
+    return kvp::KVP_OK;
+}
+
+KVP_API int kvp_read_motion_csv(const char* path, int frames, int num_tiles, float* scores,
+                                signed char* reuse) {
+    if (!path || !scores || frames <= 0 || num_tiles <= 0) return kvp::KVP_ERR_ARG;
+    return kvp::read_motion_csv(path, frames, num_tiles, scores, (int8_t*)reuse);
+}
+
+// Gather staged rows of one layer: arena[pairs[i].slot] = K[pairs[i].row] || V[...].
+KVP_API int kvp_stage_rows(const void* k, const void* v, void* arena, const int* d_pairs, int n,
+                           long long row_bytes, void* stream) {
+    kvp::GatherLayers L{};
+    L.k[0] = k;
+    L.v[0] = v;
+    L.arena[0] = arena;
+    return kvp::launch_gather_rows(L, 1, d_pairs, n, row_bytes, (cudaStream_t)stream);
+}
+
+// FP32 remapped attention over an explicit key-row span (intra, cross and
+// sliding-window in one form).  Query rows [0, T) of q/out; key rows
+// [k_lo, k_hi) of k/v with KVMap indexed by the absolute key row.
+KVP_API int kvp_attn_fp32(const float* q, const float* k, const float* v, const float* arena,
+                          const long long* kvmap, float* out, int T, int D, int heads,
+                          long long k_lo, long long k_hi, long long arena_rows, void* stream) {
+    int rc = kvp::flush_all_managers();
+    if (rc != kvp::KVP_OK) return rc;
+    int* st = kvp::status_word();
+    if (!st) return kvp::KVP_ERR_CUDA;
+    return kvp::launch_attn_fp32(q, k, v, arena, (const int64_t*)kvmap, out, T, D, heads, k_lo,
+                                 k_hi, arena_rows < 0 ? INT64_MAX : arena_rows, 1, 0, st,
+                                 (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------------ session
+
+struct kvp_session_config {
+    int mode, window, streaming, policy, frames, tokens, hidden, tile_tokens, elem_bytes, layers;
+    long long set_aside;
+};
+
+struct kvp_step_info {
+    int frame, sel_count, staged_tiles, copies;
+    long long map_row0, map_rows, window_bytes, staged_bytes;
+};
+
+KVP_API void* kvp_session_create(const kvp_session_config* c) {
+    if (!c) return nullptr;
+    kvp::SessionConfig sc{c->mode, c->window, c->streaming, c->policy, c->frames, c->tokens,
+                          c->hidden, c->tile_tokens, c->elem_bytes, c->layers, c->set_aside};
+    kvp::Session* s = new (std::nothrow) kvp::Session(sc);
+    if (!s) return nullptr;
+    if (s->status() != kvp::KVP_OK) {
+        delete s;
+        return nullptr;
+    }
+    return s;
+}
+KVP_API void kvp_session_destroy(void* s) { delete static_cast<kvp::Session*>(s); }
+KVP_API int kvp_session_plan_frame(void* s, int frame, const float* scores_flat) {
+    return static_cast<kvp::Session*>(s)->plan_frame(frame, scores_flat);
+}
+KVP_API int kvp_session_plan_stack(void* s, const float* scores_flat) {
+    return static_cast<kvp::Session*>(s)->plan_stack(scores_flat);
+}
+KVP_API int kvp_session_finish(void* s) { return static_cast<kvp::Session*>(s)->finish(); }
+KVP_API int kvp_session_info(void* s, kvp_step_info* out) {
+    if (!out) return kvp::KVP_ERR_ARG;
+    const kvp::SessionStepInfo& i = static_cast<kvp::Session*>(s)->info();
+    out->frame = i.frame;
+    out->sel_count = i.sel_count;
+    out->staged_tiles = i.staged_tiles;
+    out->copies = i.copies;
+    out->map_row0 = i.map_row0;
+    out->map_rows = i.map_rows;
+    out->window_bytes = i.window_bytes;
+    out->staged_bytes = i.staged_bytes;
+    return kvp::KVP_OK;
+}
+KVP_API long long kvp_session_slots(void* s) { return static_cast<kvp::Session*>(s)->slots(); }
+KVP_API long long kvp_session_cap_rows(void* s) { return static_cast<kvp::Session*>(s)->cap_rows(); }
+// Copies map rows [row0, row0+n) of the host KVMap.
+KVP_API int kvp_session_map(void* s, long long row0, long long n, long long* out) {
+    kvp::Session* x = static_cast<kvp::Session*>(s);
+    if (!out || row0 < 0 || n < 0 || row0 + n > x->map_len()) return kvp::KVP_ERR_ARG;
+    std::memcpy(out, x->host_map() + row0, (size_t)n * sizeof(long long));
+    return kvp::KVP_OK;
+}
+// Copies this step's (source row, arena slot) pairs; returns the count.
+KVP_API int kvp_session_copies(void* s, int* pairs_out, int cap) {
+    const auto& p = static_cast<kvp::Session*>(s)->pairs();
+    const int n = (int)(p.size() / 2);
+    if (pairs_out) std::memcpy(pairs_out, p.data(), sizeof(int) * 2 * (size_t)(n < cap ? n : cap));
+    return n;
+}
+KVP_API int kvp_session_selected(void* s, long* ids_out, int cap) {
+    const auto& v = static_cast<kvp::Session*>(s)->selected_ids();
+    const int n = (int)v.size();
+    if (ids_out) for (int i = 0; i < n && i < cap; ++i) ids_out[i] = v[(size_t)i];
+    return n;
+}
+KVP_API long long* kvp_session_device_map(void* s) {
+    return (long long*)static_cast<kvp::Session*>(s)->device_map();
+}
+KVP_API void* kvp_session_arena(void* s, int layer) {
+    return static_cast<kvp::Session*>(s)->arena(layer);
+}
+KVP_API int kvp_session_upload(void* s, void* stream) {
+    return static_cast<kvp::Session*>(s)->upload((cudaStream_t)stream);
+}
+KVP_API int kvp_session_stage(void* s, const void* const* k_layers, const void* const* v_layers,
+                              void* stream) {
+    return static_cast<kvp::Session*>(s)->stage(k_layers, v_layers, (cudaStream_t)stream);
+}
+KVP_API int kvp_session_window(void* s, int layer, void* stream) {
+    return static_cast<kvp::Session*>(s)->apply_window(layer, (cudaStream_t)stream);
+}
+KVP_API int kvp_session_clear_window(void* s, void* stream) {
+    return static_cast<kvp::Session*>(s)->clear_window((cudaStream_t)stream);
+}
+
+// --------------------------------------------------------- bf16 attention
+// tcgen05 remapped attention for one layer (see include/kvp.h for the
+// field meanings).  Staging copies queued by kvtm_* managers are issued
+// first, so they precede the kernel as in the reference.
+#include "attn_sm100.h"
+
+struct kvp_layer_io {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* out;
+    const void* arena;
+    const long long* kvmap;
+    long long q_rows, kv_rows, arena_rows;
+};
+
+struct kvp_attn_desc {
+    int tokens, frames, q_frame0, mode, window, heads, head_dim, head0, nheads, flat;
+};
+
+KVP_API int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream) {
+    if (!io || !d) return kvp::KVP_ERR_ARG;
+    int rc = kvp::flush_all_managers();
+    if (rc != kvp::KVP_OK) return rc;
+    int* st = kvp::status_word();
+    if (!st) return kvp::KVP_ERR_CUDA;
+    kvp::LayerIO L{io->q, io->k, io->v, io->out, io->arena, io->kvmap,
+                   io->q_rows, io->kv_rows, io->arena_rows};
+    kvp::AttnDesc A{d->tokens, d->frames, d->q_frame0, d->mode, d->window,
+                    d->heads, d->head_dim, d->head0, d->nheads, d->flat};
+    return kvp::launch_attn_bf16(L, A, st, (cudaStream_t)stream);
+}

@@ -1,0 +1,36 @@
+// Shared definitions for the kvp native library (B200 / sm_100a).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define KVP_API extern "C" __attribute__((visibility("default")))
+
+namespace kvp {
+
+// Status codes returned by the kvp_* entry points (0 = success).
+enum Status : int {
+    KVP_OK = 0,
+    KVP_ERR_ARG = -1,        // invalid argument (null pointer, bad shape, ...)
+    KVP_ERR_CUDA = -2,       // a CUDA runtime call failed (see kvp_last_error)
+    KVP_ERR_CAPACITY = -3,   // a fixed-size buffer would overflow
+    KVP_ERR_UNSUPPORTED = -4,// device / shape not supported by this kernel
+    KVP_ERR_TIMEOUT = -5,    // a bounded device wait expired (kernel status word)
+    KVP_ERR_MAP = -6,        // a KVMap entry pointed outside the arena
+};
+
+// Records the message of the last failure on this thread.
+void set_error(const char* fmt, ...);
+const char* last_error();
+
+// Returns KVP_ERR_CUDA and records the message when e != cudaSuccess.
+int cuda_status(cudaError_t e, const char* what);
+
+}  // namespace kvp
+
+#define KVP_CUDA(call)                                                 \
+    do {                                                               \
+        cudaError_t e_ = (call);                                       \
+        if (e_ != cudaSuccess) return ::kvp::cuda_status(e_, #call);   \
+    } while (0)

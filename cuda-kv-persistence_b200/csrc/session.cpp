@@ -1,0 +1,334 @@
+// Session implementation (see session.h).
+#include "session.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "kvp_common.h"
+
+namespace kvp {
+
+Session::Session(const SessionConfig& c)
+    : c_(c), layout_(c.tokens > 0 ? c.tokens : 1, c.tile_tokens > 0 ? c.tile_tokens : 1) {
+    if (c.frames <= 0 || c.tokens <= 0 || c.hidden <= 0 || c.tile_tokens <= 0 ||
+        (c.elem_bytes != 2 && c.elem_bytes != 4) || c.set_aside < 0 || c.layers < 0 ||
+        c.layers > kMaxLayers || c.mode < MODE_INTRA || c.mode > MODE_STACK || c.window < 0 ||
+        (2 * (int64_t)c.hidden * c.elem_bytes) % 16 != 0) {
+        set_error("session: invalid configuration");
+        status_ = KVP_ERR_ARG;
+        return;
+    }
+    nt_ = layout_.tiles_per_frame;
+    row_kv_bytes_ = (int64_t)c.hidden * c.elem_bytes;
+    // src/run_policy_experiment.cu:143-144, with the element size as a
+    // parameter (4 reproduces the reference's fp32 formula).
+    const int64_t tile_bytes = (int64_t)c.tile_tokens * row_kv_bytes_ * 2;
+    slots_ = c.set_aside / tile_bytes;
+    cap_rows_ = c.set_aside / (2 * row_kv_bytes_);
+    policy_.reset(make_policy(c.policy, (int)nt_, c.frames));
+    if (!policy_) {
+        set_error("session: unknown policy %d", c.policy);
+        status_ = KVP_ERR_ARG;
+        return;
+    }
+    mgr_.reset(new KVTileManager((size_t)c.set_aside, (size_t)c.set_aside, KVTM_FLAG_DRY_RUN));
+    mgr_->init();
+    mgr_->arena_init((size_t)c.set_aside, (size_t)(2 * row_kv_bytes_ / 4));
+    if (c.streaming) mgr_->streaming_begin();
+    map_.assign((size_t)c.frames * c.tokens, -1);
+    ids_.resize((size_t)(slots_ + (int64_t)c.frames * nt_ + 1));
+    selected_.assign((size_t)(c.frames * nt_ + 1), 0);
+    prev_selected_.assign((size_t)(c.frames * nt_ + 1), 0);
+
+    if (c.layers > 0) {
+        arena_layer_bytes_ = ((int64_t)cap_rows_ * 2 * row_kv_bytes_ + 255) / 256 * 256;
+        const size_t map_bytes = map_.size() * sizeof(int64_t);
+        const size_t pair_bytes = (size_t)std::max<int64_t>(cap_rows_, 1) * 2 * sizeof(int32_t);
+        cudaError_t e = cudaMalloc(&d_map_, map_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&d_pairs_, pair_bytes);
+        if (e == cudaSuccess && arena_layer_bytes_ > 0)
+            e = cudaMalloc(&d_arena_, (size_t)arena_layer_bytes_ * c.layers);
+        if (e == cudaSuccess) e = cudaMallocHost(&h_map_pinned_, map_bytes);
+        if (e == cudaSuccess) e = cudaMallocHost(&h_pairs_pinned_, pair_bytes);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&upload_done_, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaMemset(d_map_, 0xff, map_bytes);  // all -1
+        if (e == cudaSuccess && d_arena_)
+            e = cudaMemset(d_arena_, 0, (size_t)arena_layer_bytes_ * c.layers);
+        if (e != cudaSuccess) status_ = cuda_status(e, "session device buffers");
+    }
+}
+
+Session::~Session() {
+    if (upload_done_) { cudaEventSynchronize(upload_done_); cudaEventDestroy(upload_done_); }
+    if (d_map_) cudaFree(d_map_);
+    if (d_pairs_) cudaFree(d_pairs_);
+    if (d_arena_) cudaFree(d_arena_);
+    if (h_map_pinned_) cudaFreeHost(h_map_pinned_);
+    if (h_pairs_pinned_) cudaFreeHost(h_pairs_pinned_);
+}
+
+void* Session::arena(int layer) const {
+    if (!d_arena_ || layer < 0 || layer >= c_.layers) return nullptr;
+    return static_cast<char*>(d_arena_) + (size_t)arena_layer_bytes_ * layer;
+}
+
+int Session::stage_rows_of(int64_t gid, int64_t src_f, int64_t tile) {
+    // One tile's rows in order; a refused row stops the tile and the rows
+    // already staged stay mapped (src/run_policy_experiment.cu:197-232).
+    (void)gid;
+    const int64_t t0 = layout_.tile_start(tile);
+    const int64_t cnt = layout_.tile_count(tile);
+    bool all = true;
+    for (int64_t r = 0; r < cnt && all; ++r) {
+        const int64_t row_id = src_f * c_.tokens + t0 + r;
+        long slot = -1;
+        bool copy = false;
+        if (c_.streaming) {
+            all = mgr_->streaming_reserve((long)row_id, (size_t)(2 * row_kv_bytes_), false, &slot, &copy);
+        } else {
+            all = mgr_->arena_reserve((size_t)(2 * row_kv_bytes_), &slot);
+            copy = all;
+        }
+        if (all) {
+            map_[(size_t)row_id] = slot;
+            if (copy) {
+                pairs_.push_back((int32_t)row_id);
+                pairs_.push_back((int32_t)slot);
+            }
+        }
+    }
+    return all ? 1 : 0;
+}
+
+int Session::plan_frame(int f, const float* scores_flat) {
+    if (status_ != KVP_OK) return status_;
+    if (c_.mode == MODE_STACK || f < 0 || f >= c_.frames || !scores_flat || f != last_frame_ + 1 ||
+        finished_) {
+        set_error("plan_frame: frame %d out of order (expected %d) or wrong mode", f, last_frame_ + 1);
+        return KVP_ERR_ARG;
+    }
+    const bool cross = c_.mode == MODE_CROSS;
+    const int64_t base = (cross && c_.window > 0) ? std::max<int64_t>(0, f - c_.window + 1) : 0;
+    const int n_cand = cross ? (int)((f - base + 1) * nt_) : (int)nt_;
+    const float* cand = cross ? scores_flat + base * nt_ : scores_flat + (int64_t)f * nt_;
+    if (c_.policy == POLICY_REUSE_WEIGHTED)
+        static_cast<ReuseWeightedPolicy*>(policy_.get())->set_total_frames((int)(c_.frames - base));
+    int count = 0;
+    info_ = SessionStepInfo{};
+    info_.frame = f;
+    pairs_.clear();
+    sel_ids_.clear();
+    const bool persist = c_.policy != POLICY_NONE;
+    if (persist) {
+        policy_->select(cand, n_cand, (int)slots_, ids_.data(), &count);
+        sel_ids_.assign(ids_.begin(), ids_.begin() + std::max(0, count));
+    }
+    info_.sel_count = count;
+    const int64_t gid0 = cross ? base * nt_ : 0;
+    const int64_t sel_len = ((int64_t)f + 1) * nt_;
+    std::fill(selected_.begin(), selected_.begin() + sel_len, 0);
+    // Ids beyond the candidates (Uniform with more slots than tiles) stage
+    // nothing; the reference writes them past the end of its selection
+    // vector (src/run_policy_experiment.cu:170-172).
+    for (int i = 0; i < count; ++i)
+        if (ids_[i] >= 0 && ids_[i] < n_cand) selected_[(size_t)(gid0 + ids_[i])] = 1;
+
+    if (persist && c_.streaming && f > 0) {
+        // :173-187 -- intra mode releases with the current frame index (the
+        // reference's rows of the previous frame stay held), kept as is.
+        for (int64_t gid = 0; gid < prev_len_; ++gid) {
+            if (!prev_selected_[(size_t)gid]) continue;
+            if (gid < sel_len && selected_[(size_t)gid]) continue;
+            const int64_t src_f = cross ? gid / nt_ : f;
+            const int64_t tile = cross ? gid % nt_ : gid;
+            const int64_t t0 = layout_.tile_start(tile);
+            const int64_t cnt = layout_.tile_count(tile);
+            for (int64_t r = 0; r < cnt; ++r) mgr_->streaming_release((long)(src_f * c_.tokens + t0 + r));
+        }
+    }
+    mgr_->arena_begin_step();
+    std::fill(map_.begin(), map_.begin() + ((int64_t)f + 1) * c_.tokens, -1);
+    int tiles_ok = 0;
+    if (persist) {
+        for (int i = 0; i < count; ++i) {
+            if (ids_[i] < 0 || ids_[i] >= n_cand) continue;
+            const int64_t gid = gid0 + ids_[i];
+            const int64_t src_f = cross ? gid / nt_ : f;
+            const int64_t tile = cross ? gid % nt_ : gid;
+            tiles_ok += stage_rows_of(gid, src_f, tile);
+        }
+    }
+    info_.staged_tiles = tiles_ok;
+    info_.copies = (int)(pairs_.size() / 2);
+    info_.map_row0 = cross ? base * c_.tokens : (int64_t)f * c_.tokens;
+    info_.map_rows = cross ? ((int64_t)f + 1 - base) * c_.tokens : c_.tokens;
+    if (persist) {
+        info_.window_bytes = (int64_t)(c_.streaming ? mgr_->streaming_window_span()
+                                                    : mgr_->arena_window_span());
+        info_.staged_bytes = (int64_t)(c_.streaming ? mgr_->streaming_staged_bytes()
+                                                    : mgr_->arena_used_bytes());
+        if (c_.streaming) {
+            std::copy(selected_.begin(), selected_.begin() + sel_len, prev_selected_.begin());
+            prev_len_ = sel_len;
+        } else {
+            mgr_->arena_end_step();
+        }
+    }
+    last_frame_ = f;
+    return KVP_OK;
+}
+
+int Session::plan_stack(const float* scores_flat) {
+    if (status_ != KVP_OK) return status_;
+    if (c_.mode != MODE_STACK || !scores_flat || finished_) {
+        set_error("plan_stack: session is not in stack mode");
+        return KVP_ERR_ARG;
+    }
+    // Candidates are every frame's tiles, whatever the attention window.
+    const int64_t F = c_.frames;
+    const int64_t base = 0;
+    const int n_cand = (int)(F * nt_);
+    if (c_.policy == POLICY_REUSE_WEIGHTED)
+        static_cast<ReuseWeightedPolicy*>(policy_.get())->set_total_frames((int)(F - base));
+    int count = 0;
+    info_ = SessionStepInfo{};
+    info_.frame = -1;
+    pairs_.clear();
+    sel_ids_.clear();
+    const bool persist = c_.policy != POLICY_NONE;
+    if (persist) {
+        policy_->select(scores_flat + base * nt_, n_cand, (int)slots_, ids_.data(), &count);
+        sel_ids_.assign(ids_.begin(), ids_.begin() + std::max(0, count));
+    }
+    info_.sel_count = count;
+    const int64_t sel_len = F * nt_;
+    std::fill(selected_.begin(), selected_.begin() + sel_len, 0);
+    for (int i = 0; i < count; ++i)
+        if (ids_[i] >= 0 && ids_[i] < n_cand) selected_[(size_t)(base * nt_ + ids_[i])] = 1;
+    if (persist && c_.streaming && prev_len_ > 0) {
+        for (int64_t gid = 0; gid < prev_len_; ++gid) {
+            if (!prev_selected_[(size_t)gid] || selected_[(size_t)gid]) continue;
+            const int64_t t0 = layout_.tile_start(gid % nt_);
+            const int64_t cnt = layout_.tile_count(gid % nt_);
+            for (int64_t r = 0; r < cnt; ++r)
+                mgr_->streaming_release((long)((gid / nt_) * c_.tokens + t0 + r));
+        }
+    }
+    mgr_->arena_begin_step();
+    std::fill(map_.begin(), map_.end(), -1);
+    int tiles_ok = 0;
+    if (persist) {
+        for (int i = 0; i < count; ++i) {
+            if (ids_[i] < 0 || ids_[i] >= n_cand) continue;
+            const int64_t gid = base * nt_ + ids_[i];
+            tiles_ok += stage_rows_of(gid, gid / nt_, gid % nt_);
+        }
+    }
+    info_.staged_tiles = tiles_ok;
+    info_.copies = (int)(pairs_.size() / 2);
+    info_.map_row0 = 0;
+    info_.map_rows = F * c_.tokens;
+    if (persist) {
+        info_.window_bytes = (int64_t)(c_.streaming ? mgr_->streaming_window_span()
+                                                    : mgr_->arena_window_span());
+        info_.staged_bytes = (int64_t)(c_.streaming ? mgr_->streaming_staged_bytes()
+                                                    : mgr_->arena_used_bytes());
+        if (c_.streaming) {
+            std::copy(selected_.begin(), selected_.begin() + sel_len, prev_selected_.begin());
+            prev_len_ = sel_len;
+        } else {
+            mgr_->arena_end_step();
+        }
+    }
+    return KVP_OK;
+}
+
+int Session::finish() {
+    if (status_ != KVP_OK) return status_;
+    if (!finished_ && c_.streaming && c_.policy != POLICY_NONE) mgr_->streaming_end();
+    finished_ = true;
+    return KVP_OK;
+}
+
+int Session::upload(cudaStream_t s) {
+    if (!d_map_) return KVP_ERR_ARG;
+    const int64_t r0 = info_.map_row0, n = info_.map_rows;
+    if (r0 < 0 || n < 0 || r0 + n > (int64_t)map_.size()) return KVP_ERR_ARG;
+    // The pinned staging buffers may still feed the previous upload.
+    KVP_CUDA(cudaEventSynchronize(upload_done_));
+    std::memcpy(h_map_pinned_ + r0, map_.data() + r0, (size_t)n * sizeof(int64_t));
+    KVP_CUDA(cudaMemcpyAsync(d_map_ + r0, h_map_pinned_ + r0, (size_t)n * sizeof(int64_t),
+                             cudaMemcpyHostToDevice, s));
+    if (!pairs_.empty()) {
+        std::memcpy(h_pairs_pinned_, pairs_.data(), pairs_.size() * sizeof(int32_t));
+        KVP_CUDA(cudaMemcpyAsync(d_pairs_, h_pairs_pinned_, pairs_.size() * sizeof(int32_t),
+                                 cudaMemcpyHostToDevice, s));
+    }
+    KVP_CUDA(cudaEventRecord(upload_done_, s));
+    return KVP_OK;
+}
+
+int Session::stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s) {
+    if (!d_arena_ || !k_layers || !v_layers) return pairs_.empty() ? KVP_OK : KVP_ERR_ARG;
+    if (pairs_.empty()) return KVP_OK;
+    GatherLayers L{};
+    for (int l = 0; l < c_.layers; ++l) {
+        L.k[l] = k_layers[l];
+        L.v[l] = v_layers[l];
+        L.arena[l] = arena(l);
+    }
+    return launch_gather_rows(L, c_.layers, d_pairs_, (int)(pairs_.size() / 2), row_kv_bytes_, s);
+}
+
+int Session::apply_window(int layer, cudaStream_t s) {
+    void* a = arena(layer);
+    if (!a) return KVP_ERR_ARG;
+    cudaStreamAttrValue attr{};
+    attr.accessPolicyWindow.base_ptr = a;
+    attr.accessPolicyWindow.num_bytes = (size_t)info_.window_bytes;
+    attr.accessPolicyWindow.hitRatio = info_.window_bytes > 0 ? 1.0f : 0.0f;
+    attr.accessPolicyWindow.hitProp =
+        info_.window_bytes > 0 ? cudaAccessPropertyPersisting : cudaAccessPropertyNormal;
+    attr.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+    if (info_.window_bytes <= 0) attr.accessPolicyWindow.missProp = cudaAccessPropertyNormal;
+    KVP_CUDA(cudaStreamSetAttribute(s, cudaStreamAttributeAccessPolicyWindow, &attr));
+    return KVP_OK;
+}
+
+int Session::clear_window(cudaStream_t s) {
+    cudaStreamAttrValue attr{};
+    attr.accessPolicyWindow.base_ptr = nullptr;
+    attr.accessPolicyWindow.num_bytes = 0;
+    attr.accessPolicyWindow.hitRatio = 0.f;
+    attr.accessPolicyWindow.hitProp = cudaAccessPropertyNormal;
+    attr.accessPolicyWindow.missProp = cudaAccessPropertyNormal;
+    KVP_CUDA(cudaStreamSetAttribute(s, cudaStreamAttributeAccessPolicyWindow, &attr));
+    return KVP_OK;
+}
+
+int read_motion_csv(const char* path, int frames, int num_tiles, float* scores, int8_t* reuse) {
+    FILE* f = std::fopen(path, "r");
+    if (!f) return -1;
+    std::memset(scores, 0, sizeof(float) * (size_t)frames * (size_t)num_tiles);
+    if (reuse) std::memset(reuse, 0, (size_t)frames * (size_t)num_tiles);
+    char line[256];
+    int accepted = 0;
+    if (std::fgets(line, sizeof line, f)) {  // header
+        while (std::fgets(line, sizeof line, f)) {
+            int fr = 0, tid = 0, is_static = 0, start = 0, count = 0, rz = 0;
+            float score = 0.f;
+            const int got = std::sscanf(line, "%d,%d,%f,%d,%d,%d,%d", &fr, &tid, &score, &is_static,
+                                        &start, &count, &rz);
+            if ((got == 6 || got == 7) && fr >= 0 && fr < frames && tid >= 0 && tid < num_tiles) {
+                scores[(size_t)fr * num_tiles + tid] = score;
+                if (got == 7 && reuse) reuse[(size_t)fr * num_tiles + tid] = (int8_t)rz;
+                ++accepted;
+            }
+        }
+    }
+    std::fclose(f);
+    return accepted;
+}
+
+}  // namespace kvp

@@ -1,0 +1,127 @@
+// Session: the per-frame admission loop that turns policy selections into a
+// KVMap plus a list of rows to stage, i.e. the host hot loop of the
+// reference driver (src/run_policy_experiment.cu:156-274) as a library.
+//
+// Per step (one query frame, or the whole stack): select -> release rows of
+// tiles that dropped out (streaming) -> stage the selected tiles' rows in
+// policy order -> KVMap[row] = arena slot.  Admission, slot numbers and byte
+// counts are bit-exact with the reference for intra and cross modes; the
+// sliding window (cross, window > 0) and the stack mode are extensions
+// defined in DESIGN.md terms below:
+//   * window W: frame f's candidates are the tiles of frames
+//     [max(0, f-W+1), f]; ReuseWeighted counts remaining sweeps from that
+//     first frame (total_frames - base); ids are offset to absolute gids;
+//   * stack: one admission over all frames' tiles (the cross step of the last
+//     frame), one KVMap shared by every query frame of a causal stack.
+// The device side keeps one arena per layer (all layers share the admission:
+// motion scores are per tile, not per layer) and stages every layer's rows
+// with one gather launch.
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "kv_tile_manager.h"
+#include "tile_gating_policy.h"
+#include "tile_layout.h"
+
+namespace kvp {
+
+enum SessionMode { MODE_INTRA = 0, MODE_CROSS = 1, MODE_STACK = 2 };
+
+struct SessionConfig {
+    int mode;         // SessionMode
+    int window;       // cross/stack: 0 = full causal prefix, W > 0 = last W frames
+    int streaming;    // 0 dense arena, 1 sticky streaming slots
+    int policy;       // PolicyId
+    int frames;
+    int tokens;       // tokens per frame
+    int hidden;       // D = heads * head_dim
+    int tile_tokens;
+    int elem_bytes;   // 4 = fp32 (reference accounting), 2 = bf16
+    int layers;       // arenas kept on device (0 = plan only)
+    int64_t set_aside;// persisting budget in bytes; also the arena capacity per layer
+};
+
+struct SessionStepInfo {
+    int frame;            // -1 for a stack step
+    int sel_count;        // raw policy count
+    int staged_tiles;
+    int copies;           // rows to stage this step
+    int64_t map_row0;     // first KVMap row the kernel reads
+    int64_t map_rows;     // rows the kernel reads
+    int64_t window_bytes; // persisting window span, 0 when none
+    int64_t staged_bytes; // streaming: cumulative; dense: arena bytes used this step
+};
+
+class Session {
+public:
+    explicit Session(const SessionConfig& c);
+    ~Session();
+    int status() const { return status_; }  // KVP_OK after construction
+
+    // Host planning (no GPU needed).
+    int plan_frame(int f, const float* scores_flat);  // intra / cross
+    int plan_stack(const float* scores_flat);         // stack
+    const SessionStepInfo& info() const { return info_; }
+    const int64_t* host_map() const { return map_.data(); }
+    const std::vector<int32_t>& pairs() const { return pairs_; }  // (row, slot) interleaved
+    const std::vector<long>& selected_ids() const { return sel_ids_; }
+    int64_t slots() const { return slots_; }
+    int64_t cap_rows() const { return cap_rows_; }
+    int64_t map_len() const { return (int64_t)map_.size(); }
+    int finish();  // streaming_end / final demote (same as the driver's end of run)
+
+    // Device side (layers > 0).
+    int64_t* device_map() const { return d_map_; }
+    void* arena(int layer) const;
+    int64_t arena_layer_bytes() const { return arena_layer_bytes_; }
+    // Uploads this step's map slice and copy list (pinned staging, async).
+    int upload(cudaStream_t s);
+    // Gathers this step's rows into every layer's arena.
+    int stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s);
+    // Persisting window over layer's arena span (or a normal-property
+    // window when this step has no span).
+    int apply_window(int layer, cudaStream_t s);
+    int clear_window(cudaStream_t s);
+
+private:
+    int stage_rows_of(int64_t gid, int64_t src_frame, int64_t tile);
+
+    SessionConfig c_;
+    TileLayout layout_;
+    std::unique_ptr<TileGatingPolicy> policy_;
+    std::unique_ptr<KVTileManager> mgr_;  // dry-run accounting
+    int status_ = 0;
+    int64_t nt_ = 0, slots_ = 0, cap_rows_ = 0, row_kv_bytes_ = 0;
+    std::vector<int64_t> map_;
+    std::vector<int32_t> pairs_;
+    std::vector<long> ids_;
+    std::vector<long> sel_ids_;
+    std::vector<char> selected_, prev_selected_;
+    int64_t prev_len_ = 0;
+    int last_frame_ = -1;
+    bool finished_ = false;
+    SessionStepInfo info_{};
+
+    // device
+    int64_t* d_map_ = nullptr;
+    int32_t* d_pairs_ = nullptr;
+    void* d_arena_ = nullptr;
+    int64_t arena_layer_bytes_ = 0;
+    int64_t* h_map_pinned_ = nullptr;
+    int32_t* h_pairs_pinned_ = nullptr;
+    cudaEvent_t upload_done_ = nullptr;
+};
+
+// Reference motion CSV reader (src/run_policy_experiment.cu:45-69): rows
+// "frame,tile,score,is_static,start,count[,reuse]", score parsed as "%f";
+// absent entries stay 0.  Returns accepted rows, or -1 if unreadable.
+int read_motion_csv(const char* path, int frames, int num_tiles, float* scores,
+                    int8_t* reuse);
+
+}  // namespace kvp

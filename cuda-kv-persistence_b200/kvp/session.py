@@ -1,0 +1,121 @@
+"""Session: the per-frame KVMap / admission emitter over the C ABI.
+
+Mirrors the host loop of src/run_policy_experiment.cu:156-274 (select ->
+release -> stage -> KVMap) for intra, cross (optionally windowed) and
+whole-stack modes.  With ``layers=0`` it only plans on the host (no GPU).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import KvpError, SessionConfig, StepInfo, check, lib
+from .policies import POLICIES
+
+MODES = {"intra": 0, "cross": 1, "stack": 2}
+
+
+@dataclass
+class Step:
+    frame: int
+    sel_count: int
+    staged_tiles: int
+    copies: int
+    map_row0: int
+    map_rows: int
+    window_bytes: int
+    staged_bytes: int
+
+
+class Session:
+    def __init__(self, *, mode="cross", policy="recency", frames, tokens=1560, hidden=1536,
+                 tile_tokens=16, elem_bytes=2, set_aside=2162688, streaming=False, window=0,
+                 layers=0):
+        cfg = SessionConfig(MODES[mode], window, int(streaming),
+                            POLICIES[policy] if isinstance(policy, str) else int(policy), frames,
+                            tokens, hidden, tile_tokens, elem_bytes, layers, set_aside)
+        self._L = lib()
+        self.h = self._L.kvp_session_create(C.byref(cfg))
+        if not self.h:
+            raise KvpError("kvp_session_create failed: " + self._L.kvp_last_error().decode())
+        self.mode, self.frames, self.tokens, self.hidden = mode, frames, tokens, hidden
+        self.layers = layers
+        self.map_len = frames * tokens
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._L.kvp_session_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def slots(self) -> int:
+        return int(self._L.kvp_session_slots(self.h))
+
+    @property
+    def cap_rows(self) -> int:
+        return int(self._L.kvp_session_cap_rows(self.h))
+
+    def plan_frame(self, frame: int, scores_flat: np.ndarray) -> Step:
+        s = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
+        check(self._L.kvp_session_plan_frame(self.h, frame, s.ctypes.data), "plan_frame")
+        return self.info()
+
+    def plan_stack(self, scores_flat: np.ndarray) -> Step:
+        s = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
+        check(self._L.kvp_session_plan_stack(self.h, s.ctypes.data), "plan_stack")
+        return self.info()
+
+    def finish(self):
+        check(self._L.kvp_session_finish(self.h), "finish")
+
+    def info(self) -> Step:
+        i = StepInfo()
+        check(self._L.kvp_session_info(self.h, C.byref(i)), "info")
+        return Step(i.frame, i.sel_count, i.staged_tiles, i.copies, i.map_row0, i.map_rows,
+                    i.window_bytes, i.staged_bytes)
+
+    def host_map(self, row0: int = 0, n: int | None = None) -> np.ndarray:
+        n = self.map_len - row0 if n is None else n
+        out = np.empty(n, dtype=np.int64)
+        check(self._L.kvp_session_map(self.h, row0, n, out.ctypes.data), "map")
+        return out
+
+    def copies(self) -> np.ndarray:
+        n = self._L.kvp_session_copies(self.h, None, 0)
+        out = np.empty((max(n, 1), 2), dtype=np.int32)
+        self._L.kvp_session_copies(self.h, out.ctypes.data, n)
+        return out[:n]
+
+    def selected(self) -> np.ndarray:
+        n = self._L.kvp_session_selected(self.h, None, 0)
+        out = np.empty(max(n, 1), dtype=np.int64)
+        self._L.kvp_session_selected(self.h, out.ctypes.data, n)
+        return out[:n]
+
+    # device side ------------------------------------------------------
+    def device_map_ptr(self) -> int:
+        return int(self._L.kvp_session_device_map(self.h) or 0)
+
+    def arena_ptr(self, layer: int) -> int:
+        return int(self._L.kvp_session_arena(self.h, layer) or 0)
+
+    def upload(self, stream: int = 0):
+        check(self._L.kvp_session_upload(self.h, C.c_void_p(stream)), "upload")
+
+    def stage(self, k_ptrs, v_ptrs, stream: int = 0):
+        n = len(k_ptrs)
+        ka = (C.c_void_p * n)(*k_ptrs)
+        va = (C.c_void_p * n)(*v_ptrs)
+        check(self._L.kvp_session_stage(self.h, ka, va, C.c_void_p(stream)), "stage")
+
+    def window(self, layer: int, stream: int = 0):
+        check(self._L.kvp_session_window(self.h, layer, C.c_void_p(stream)), "window")
+
+    def clear_window(self, stream: int = 0):
+        check(self._L.kvp_session_clear_window(self.h, C.c_void_p(stream)), "clear_window")

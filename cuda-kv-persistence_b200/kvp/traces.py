@@ -1,0 +1,161 @@
+"""Synthetic inputs and the motion-trace CSV format.
+
+* ``reference_synthetic_trace`` restates the reference's synthetic trace
+  generator (traces/gen_synthetic_motion.py:41-89 scores, :125-171 Q/K/V
+  with motion-coupled K/V drift) with the same constants and the same draw
+  order from one seeded torch.Generator, so seed 42 / 8 frames reproduces
+  the reference's trace_meta_8f.json and golden_meta.json statistics.
+* ``motion_config{1..5}`` are the seeded motion generators of the BASELINE
+  configs (new; defined in DESIGN.md).  Each uses its own
+  ``torch.Generator().manual_seed(seed)``; Q/K/V come from ``qkv``.
+* ``write_motion_csv`` writes the reference CSV
+  (frame_id,tile_id,motion_score,is_static,token_start,token_count) with
+  6-decimal scores, the text the reference driver parses with "%f".
+"""
+
+from __future__ import annotations
+
+import math
+from pathlib import Path
+
+import numpy as np
+import torch
+
+TOKENS, HIDDEN, HEADS, HEAD_DIM, TILE = 1560, 1536, 12, 128, 16
+
+# traces/gen_synthetic_motion.py:32-39
+_STATIC_MEAN, _STATIC_STD, _STATIC_JITTER = 0.05, 0.02, 0.01
+_MOVING_MEAN, _MOVING_STD, _MOVING_WALK = 1.5, 0.4, 0.25
+_MOVING_CLIP = (0.8, 4.0)
+_KV_DRIFT = 0.15
+
+
+def tile_counts(tokens: int = TOKENS, tile_tokens: int = TILE) -> np.ndarray:
+    full, rem = divmod(tokens, tile_tokens)
+    c = [tile_tokens] * full + ([rem] if rem else [])
+    return np.asarray(c, dtype=np.int64)
+
+
+def reference_synthetic_trace(frames: int = 8, seed: int = 42, frac_static: float = 0.65,
+                              tokens: int = TOKENS, hidden: int = HIDDEN,
+                              tile_tokens: int = TILE):
+    """(scores [F, tiles] f32, is_static [tiles] bool, Q, K, V [F, T, D] f32 numpy)."""
+    g = torch.Generator().manual_seed(seed)
+    counts = torch.from_numpy(tile_counts(tokens, tile_tokens))
+    n = counts.numel()
+    # motion: regime flag, static base, moving start, then per-frame jitter/walk pairs
+    is_static = torch.rand(n, generator=g) < frac_static
+    static0 = (_STATIC_MEAN + _STATIC_STD * torch.randn(n, generator=g)).clamp(min=0.005)
+    moving0 = (_MOVING_MEAN + _MOVING_STD * torch.randn(n, generator=g)).clamp(*_MOVING_CLIP)
+    scores = torch.empty(frames, n)
+    scores[0] = torch.where(is_static, static0, moving0)
+    for f in range(1, frames):
+        jitter = _STATIC_JITTER * torch.randn(n, generator=g)
+        walk = _MOVING_WALK * torch.randn(n, generator=g)
+        scores[f] = torch.where(is_static, (scores[f - 1] + jitter).clamp(min=0.0),
+                                (scores[f - 1] + walk).clamp(*_MOVING_CLIP))
+    # Q, then K0, V0, then per frame K and V drift scaled by the tile's motion
+    per_token = torch.repeat_interleave(scores, counts, dim=1)
+    q = torch.randn(frames, tokens, hidden, generator=g)
+    k = torch.empty(frames, tokens, hidden)
+    v = torch.empty(frames, tokens, hidden)
+    k[0] = torch.randn(tokens, hidden, generator=g)
+    v[0] = torch.randn(tokens, hidden, generator=g)
+    for f in range(1, frames):
+        scale = _KV_DRIFT * per_token[f].unsqueeze(1)
+        k[f] = k[f - 1] + scale * torch.randn(tokens, hidden, generator=g)
+        v[f] = v[f - 1] + scale * torch.randn(tokens, hidden, generator=g)
+    return scores.numpy(), is_static.numpy(), q.numpy(), k.numpy(), v.numpy()
+
+
+def write_motion_csv(path, scores: np.ndarray, is_static=None, tokens: int = TOKENS,
+                     tile_tokens: int = TILE) -> Path:
+    scores = np.asarray(scores, dtype=np.float32)
+    frames, n = scores.shape
+    counts = tile_counts(tokens, tile_tokens)
+    starts = np.cumsum(counts) - counts
+    if is_static is None:
+        is_static = np.zeros(n, dtype=bool)
+    lines = ["frame_id,tile_id,motion_score,is_static,token_start,token_count"]
+    for f in range(frames):
+        for t in range(n):
+            lines.append(f"{f},{t},{float(scores[f, t]):.6f},{int(is_static[t])},"
+                         f"{int(starts[t])},{int(counts[t])}")
+    p = Path(path)
+    p.write_text("\n".join(lines) + "\n")
+    return p
+
+
+def read_motion_csv(path, frames: int, num_tiles: int) -> np.ndarray:
+    """Scores exactly as the reference parses them (sscanf %f), via the C ABI."""
+    from ._lib import lib
+    s = np.zeros((frames, num_tiles), dtype=np.float32)
+    n = lib().kvp_read_motion_csv(str(path).encode(), frames, num_tiles, s.ctypes.data, None)
+    if n < 0:
+        raise FileNotFoundError(path)
+    return s
+
+
+def csv_round_trip(scores: np.ndarray, workdir) -> np.ndarray:
+    """Scores after the CSV text round trip the reference driver applies."""
+    p = Path(workdir) / "motion_trace.csv"
+    write_motion_csv(p, scores)
+    return read_motion_csv(p, *np.asarray(scores).shape)
+
+
+# ---------------------------------------------------------------- BASELINE configs
+def motion_config1(seed: int = 0, tiles: int = 98) -> np.ndarray:
+    """Config 1: one frame, U[0,1) per tile."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.rand(1, tiles, generator=g).numpy()
+
+
+def motion_config2(frames: int = 8, seed: int = 0, tiles: int = 98, rho: float = 0.9,
+                   sigma: float = 0.1) -> np.ndarray:
+    """Config 2: AR(1) per tile, m_0 ~ U[0,1), m_f = clamp(rho m_{f-1} + N(0, sigma^2), 0, 1)."""
+    g = torch.Generator().manual_seed(seed)
+    m = torch.empty(frames, tiles)
+    m[0] = torch.rand(tiles, generator=g)
+    for f in range(1, frames):
+        m[f] = (rho * m[f - 1] + sigma * torch.randn(tiles, generator=g)).clamp(0.0, 1.0)
+    return m.numpy()
+
+
+def motion_config3(frames: int = 50, seed: int = 0, tiles: int = 98, blob_frac: float = 0.2):
+    """Config 3: background U[0,0.1); a blob of round(0.2*tiles) consecutive
+    tile ids with motion U[0.9,1.0] starting at tile f (mod tiles): it
+    translates one tile per frame."""
+    g = torch.Generator().manual_seed(seed)
+    m = 0.1 * torch.rand(frames, tiles, generator=g)
+    blob = int(round(blob_frac * tiles))
+    hot = 0.9 + 0.1 * torch.rand(frames, blob, generator=g)
+    for f in range(frames):
+        idx = (torch.arange(blob) + f) % tiles
+        m[f, idx] = hot[f]
+    return m.numpy()
+
+
+def motion_config4(frames: int = 21, seed: int = 0, tiles: int = 98) -> np.ndarray:
+    """Config 4 (no motion model given): U[0,1) per tile and frame."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.rand(frames, tiles, generator=g).numpy()
+
+
+def motion_config5(regime: str, frames: int = 16, seed: int = 0, tiles: int = 98) -> np.ndarray:
+    """Config 5: 'static' U[0,0.05) or 'high' U[0,1) i.i.d. per tile and frame."""
+    g = torch.Generator().manual_seed(seed)
+    u = torch.rand(frames, tiles, generator=g)
+    return (0.05 * u if regime == "static" else u).numpy()
+
+
+def qkv(rows: int, hidden: int = HIDDEN, *, seed: int = 0, dtype=torch.bfloat16,
+        device="cpu", head_dim: int = HEAD_DIM):
+    """Q, K, V ~ N(0,1)/sqrt(head_dim), [rows, hidden], from one generator on
+    `device` (drawn in fp32, then cast)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    s = 1.0 / math.sqrt(head_dim)
+    out = []
+    for _ in range(3):
+        t = torch.randn(rows, hidden, generator=g, device=device, dtype=torch.float32) * s
+        out.append(t.to(dtype))
+    return tuple(out)

@@ -1,0 +1,134 @@
+/* libkvp.so: B200 additions to the reference interface (no torch types).
+ *
+ * Everything here extends GauthamMK-0/cuda-kv-persistence's surface; the
+ * drop-in entry points themselves are in kv_tile_manager.h and
+ * attn_kernel.h.  All kvp_* functions return 0 on success or a negative
+ * status (-1 argument, -2 CUDA, -3 capacity, -4 unsupported, -5 timeout,
+ * -6 KVMap out of range); kvp_last_error() describes the last failure on
+ * the calling thread.  Streams are cudaStream_t passed as void*.
+ */
+#ifndef KVP_H
+#define KVP_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+const char* kvp_version(void);
+const char* kvp_last_error(void);
+
+/* Device status word written by the kernels: bit 0 = a KVMap entry pointed
+ * outside the arena (the base row was read instead), bit 1 = a bounded
+ * device wait expired.  Synchronises `stream`, returns and clears it. */
+int kvp_read_status(void* stream);
+
+typedef struct {
+    int device, sm_count, cc_major, cc_minor;
+    long long l2_bytes;
+    long long max_persisting_l2_bytes;        /* cudaDevAttrMaxPersistingL2CacheSize */
+    long long max_access_policy_window_bytes; /* cudaDevAttrMaxAccessPolicyWindowSize */
+    long long persisting_limit_bytes;         /* current cudaLimitPersistingL2CacheSize */
+    long long hbm_bytes;
+} kvp_device_info;
+/* device < 0: the current device.  Replaces the hard-coded RTX 3060 values
+ * of the reference's configs/grounding_config.json and its probe
+ * src/l2_persist_smoke.cu:20-35. */
+int kvp_query_device(int device, kvp_device_info* out);
+
+/* TileGatingPolicy::select by id, src/tile_gating_policy.h:14-15
+ * (0 none, 1 uniform, 2 recency, 3 motion, 4 reuse_weighted; tiles_per_frame
+ * and total_frames parameterise reuse_weighted as in its constructor,
+ * src/tile_gating_policy.h:51). */
+int tgp_select(int policy, const float* scores, int n, int max_tiles, int tiles_per_frame,
+               int total_frames, long* out_ids, int* out_count);
+
+/* Motion CSV reader, src/run_policy_experiment.cu:45-69: scores [frames][num_tiles],
+ * reuse (may be NULL) [frames][num_tiles]. Returns accepted rows or -1. */
+int kvp_read_motion_csv(const char* path, int frames, int num_tiles, float* scores,
+                        signed char* reuse);
+
+/* Vectorised arena compaction (replaces the 2 cudaMemcpyAsync per row of
+ * src/kv_tile_manager.cu:111-116): for i < n,
+ * arena[pairs[2i+1]] = K[pairs[2i]] || V[pairs[2i]], rows of row_bytes
+ * (multiple of 16) bytes; d_pairs is device memory. */
+int kvp_stage_rows(const void* k, const void* v, void* arena, const int* d_pairs, int n,
+                   long long row_bytes, void* stream);
+
+/* FP32 remapped attention over an explicit key span (intra, cross and
+ * sliding window in one form): query rows [0, T) of q/out, key rows
+ * [k_lo, k_hi) of k/v, kvmap indexed by the absolute key row; map entries
+ * >= arena_rows are reported in kvp_read_status (arena_rows < 0: unchecked).
+ * src/gated_attention_kernel.cu:34-139. */
+int kvp_attn_fp32(const float* q, const float* k, const float* v, const float* arena,
+                  const long long* kvmap, float* out, int T, int D, int heads, long long k_lo,
+                  long long k_hi, long long arena_rows, void* stream);
+
+/* ---- BF16 tcgen05 remapped attention (sm_100a) ---------------------------
+ * Same semantics as attn_forward_kernel (src/gated_attention_kernel.cu:34-139)
+ * in bf16 with fp32 accumulation, for one layer and any set of heads. */
+typedef struct {
+    const void* q;          /* bf16 [q_rows][D], D = heads*128 */
+    const void* k;          /* bf16 [kv_rows][D] */
+    const void* v;          /* bf16 [kv_rows][D] */
+    void* out;              /* bf16 [q_rows][D] */
+    const void* arena;      /* bf16 [arena_rows][2*D] (K half, V half) or NULL */
+    const long long* kvmap; /* int64 [kv_rows], absolute key rows, or NULL */
+    long long q_rows, kv_rows, arena_rows;
+} kvp_layer_io;
+
+typedef struct {
+    int tokens;    /* rows per frame (T) */
+    int frames;    /* query frames [q_frame0, q_frame0 + frames) */
+    int q_frame0;
+    int mode;      /* 0 intra (keys of the same frame), 1 causal cross-frame */
+    int window;    /* causal: 0 = frames 0..f, W = frames max(0,f-W+1)..f */
+    int heads;
+    int head_dim;  /* 128 */
+    int head0;     /* heads [head0, head0 + nheads) */
+    int nheads;
+    int flat;      /* causal, window 0: 128-row query tiles across frame edges */
+} kvp_attn_desc;
+
+int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
+
+/* ---- Session: the per-frame admission loop / KVMap emitter of
+ * src/run_policy_experiment.cu:156-274 as a library. */
+typedef struct {
+    int mode;        /* 0 intra, 1 cross, 2 stack (one admission for all frames) */
+    int window;      /* cross: 0 = full prefix, W = candidates of the last W frames */
+    int streaming;   /* 0 dense arena, 1 sticky streaming slots */
+    int policy;      /* as tgp_select */
+    int frames, tokens, hidden, tile_tokens;
+    int elem_bytes;  /* 4 fp32 (the reference's accounting), 2 bf16 */
+    int layers;      /* device arenas to keep (0 = host planning only, no GPU needed) */
+    long long set_aside; /* persisting budget in bytes = arena capacity per layer */
+} kvp_session_config;
+
+typedef struct {
+    int frame, sel_count, staged_tiles, copies;
+    long long map_row0, map_rows, window_bytes, staged_bytes;
+} kvp_step_info;
+
+void* kvp_session_create(const kvp_session_config* c);
+void kvp_session_destroy(void* s);
+int kvp_session_plan_frame(void* s, int frame, const float* scores_flat); /* intra / cross */
+int kvp_session_plan_stack(void* s, const float* scores_flat);            /* stack */
+int kvp_session_finish(void* s);
+int kvp_session_info(void* s, kvp_step_info* out);
+long long kvp_session_slots(void* s);
+long long kvp_session_cap_rows(void* s);
+int kvp_session_map(void* s, long long row0, long long n, long long* out);
+int kvp_session_copies(void* s, int* pairs_out, int cap);
+int kvp_session_selected(void* s, long* ids_out, int cap);
+long long* kvp_session_device_map(void* s);
+void* kvp_session_arena(void* s, int layer);
+int kvp_session_upload(void* s, void* stream);
+int kvp_session_stage(void* s, const void* const* k_layers, const void* const* v_layers,
+                      void* stream);
+int kvp_session_window(void* s, int layer, void* stream);
+int kvp_session_clear_window(void* s, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
