@@ -1,0 +1,447 @@
+"""Benchmark: remapped-MHA TFLOP/s on the Wan2.1-1.3B-shaped causal stack.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kvp|reference]
+
+Workload: 21 latent frames x 1560 tokens = 32,760 tokens,
+30 layers x 12 heads x 128 (hidden 1536), bf16, Q/K/V ~ N(0,1)/sqrt(128),
+block-causal by frame.  The 360 (layer, head) pairs are split into
+contiguous blocks over the ranks (fixed total work: strong scaling); each
+rank runs its pairs through the remapped-attention path and the per-rank
+outputs are all-gathered over NVLink (NCCL) on a separate stream, one step
+behind, so the transfer overlaps the next step's compute.
+
+One step = one stack admission (ReuseWeighted over all 21*98 tiles, budget
+= this GPU's cudaDevAttrMaxPersistingL2CacheSize), KVMap upload, one
+compaction launch into every layer's arena, then per layer a persisting
+window and one tcgen05 attention launch (1.0362e14 FLOP over 360 pairs,
+counted on real tokens only).  The inputs (12.1 GB) exceed the 126 MB L2,
+so no explicit flush is needed between steps.
+
+Printed JSON keys follow the driver contract; `value` times device-resident
+inputs, `e2e` times the same work through the public API with host buffers
+(pinned H2D of Q/K/V and D2H of O every step, pipelined per layer chunk).
+`--impl reference` times the reference's CPU path (the golden attention of
+traces/gen_golden.py, here the oracle's numpy port) on all host threads over
+a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "cuda-kv-persistence_b200"
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(PKG))
+
+FRAMES, TOKENS, LAYERS, HEADS, HEAD_DIM = 21, 1560, 30, 12, 128
+N_PAIRS = LAYERS * HEADS
+METRIC = "remapped-MHA TFLOP/s"
+KERNEL = "attn_bf16_sm100_kernel"
+
+
+def stack_flops(frames=FRAMES, tokens=TOKENS, pairs=N_PAIRS):
+    return float(sum(4 * tokens * (f + 1) * tokens * HEAD_DIM for f in range(frames)) * pairs)
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops_sustained") or d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
+    return 1400.0, 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram read+write bytes per attention launch from the committed ncu summary."""
+    for p in sorted((ROOT / "profiles").glob("*.md")):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+        if m and "stack21" in p.name:
+            return float(m.group(1))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, r[5:9]):
+                if "Active" in val and "Not" not in val:
+                    reasons.add(n)
+        if not sm:
+            return None
+        busy = [x for x in sm if x > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU arms
+def cpu_attention_sample(seconds: float = 12.0, max_heads: int = HEADS, seed: int = 0):
+    """Oracle port of the reference golden (numpy, all host threads) on whole
+    (layer 0, head h) pairs of the stack, heads taken until `seconds` pass."""
+    import numpy as np
+    import torch
+    from oracle.attention import attention_frames
+    rows = FRAMES * TOKENS
+    done_flops, t_total, heads_done = 0.0, 0.0, 0
+    per_pair = stack_flops(pairs=1)
+    for h in range(max_heads):
+        g = torch.Generator().manual_seed(seed * 1_000_003 + h)
+        s = HEAD_DIM ** -0.5
+        q, k, v = ((torch.randn(rows, HEAD_DIM, generator=g) * s).to(torch.bfloat16).float().numpy()
+                   for _ in range(3))
+        t0 = time.perf_counter()
+        attention_frames(q, k, v, frames=FRAMES, tokens=TOKENS, heads=1, head_dim=HEAD_DIM,
+                         mode="cross")
+        t_total += time.perf_counter() - t0
+        done_flops += per_pair
+        heads_done += 1
+        if t_total >= seconds:
+            break
+    return done_flops / t_total / 1e12, heads_done, t_total
+
+
+def run_reference(args, rank: int, world: int) -> int:
+    if rank != 0:
+        return 0
+    import numpy as np  # noqa: F401
+    cores = os.cpu_count() or 1
+    # One step = one whole (layer, head) pair, all 21 query frames.
+    for _ in range(args.warmup):
+        cpu_attention_sample(seconds=0.0, max_heads=1)
+    t_steps = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_attention_sample(seconds=0.0, max_heads=1, seed=i)
+        t_steps.append(time.perf_counter() - t0)
+    per = stack_flops(pairs=1)
+    ms = 1e3 * sum(t_steps) / len(t_steps)
+    val = per / (ms / 1e3) / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "wan21_stack_21f_30L_12H_causal", "frames": FRAMES,
+                   "tokens_per_frame": TOKENS, "layers": LAYERS, "heads": HEADS,
+                   "head_dim": HEAD_DIM, "sample": "one (layer, head) pair, 21 query frames"},
+        "cpu_baseline": {"value": round(val, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": "one (layer, head) pair per step, 21 query frames, "
+                                   "traces/gen_golden.py attention_reference_cross math (numpy)"},
+        "e2e": {"value": round(val, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from kvp import traces
+    from kvp._lib import DeviceInfo, lib
+    from kvp.stack import StackRank, pair_range
+    import ctypes as C
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    info = DeviceInfo()
+    lib().kvp_query_device(local_rank, C.byref(info))
+    set_aside = args.set_aside or int(info.max_persisting_l2_bytes)
+    p0, p1 = pair_range(rank, world, N_PAIRS)
+    stack = StackRank(p0=p0, p1=p1, heads=HEADS, frames=FRAMES, tokens=TOKENS,
+                      policy=args.policy, set_aside=set_aside, device=dev, seed=args.seed)
+    with tempfile.TemporaryDirectory() as td:
+        scores = traces.csv_round_trip(traces.motion_config4(frames=FRAMES, seed=args.seed), td)
+    stream = torch.cuda.Stream(device=dev)
+    sp = int(stream.cuda_stream)
+    comm = torch.cuda.Stream(device=dev) if world > 1 else None
+
+    # outputs: two flat buffers per rank (the gather of step s overlaps step s+1)
+    local_elems = sum(c.o.numel() for c in stack.chunks)
+    flat = [torch.empty(local_elems, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    gathered = (torch.empty(local_elems * world, dtype=torch.bfloat16, device=dev)
+                if world > 1 else None)
+
+    def bind_outputs(buf):
+        off = 0
+        for c in stack.chunks:
+            n = c.o.numel()
+            c.o = buf[off:off + n].view(c.o.shape)
+            off += n
+
+    launches_per_step = len(stack.chunks) + (len(stack.sessions) if stack.persist else 0)
+    attn_events = []
+    gather_done = [None, None]   # last all-gather that read each output buffer
+
+    def one_step(s_idx: int, timed: bool):
+        b = s_idx & 1
+        if gather_done[b] is not None:
+            stream.wait_event(gather_done[b])   # step s-2's gather has read this buffer
+        bind_outputs(flat[b])
+        with torch.cuda.stream(stream):
+            stack.plan_and_stage(scores, sp)
+            for c in stack.chunks:
+                if timed:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                stack.attend(c, sp)
+                if timed:
+                    e1.record(stream)
+                    attn_events.append((e0, e1))
+            if stack.persist:
+                stack.sessions[0].clear_window(sp)
+        if world > 1:
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            comm.wait_event(ev)
+            with torch.cuda.stream(comm):
+                dist.all_gather_into_tensor(gathered, flat[b])
+            done = torch.cuda.Event()
+            done.record(comm)
+            gather_done[b] = done
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+            torch.cuda.synchronize(dev)
+
+    for i in range(args.warmup):
+        one_step(i, False)
+    barrier()
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        one_step(args.warmup + i, True)
+    if world > 1:
+        stream.wait_stream(comm)
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = t0.elapsed_time(t1) / args.steps
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn_events)
+    n_attn = len(attn_events)
+    status = lib().kvp_read_status(C.c_void_p(sp))
+    if world > 1:
+        t = torch.tensor([ms, attn_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, attn_ms = float(t[0]), float(t[1])
+        st = torch.tensor([status], device=dev, dtype=torch.int32)
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        status = int(st[0])
+    total_flops = stack_flops()
+    value = total_flops / (ms / 1e3) / 1e12
+
+    # ---------------- e2e through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, stack, scores, dev, stream, world, local_rank)
+
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    result = 0
+    if rank == 0:
+        peak, hbm, peak_kind = measured_peaks()
+        local_attn_flops = stack.flops() * args.steps
+        achieved = local_attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms > 0 else None
+        per_launch_flops = local_attn_flops / max(n_attn, 1)
+        roofline = {"bound": "tensor", "achieved": round(achieved, 2) if achieved else None,
+                    "peak": peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4) if achieved else None,
+                    "traffic": profiled_traffic(), "kernel": KERNEL,
+                    "peak_kind": f"{peak_kind} bf16 sustained (cuBLAS)",
+                    "flop_per_launch": per_launch_flops,
+                    "avg_launch_ms": round(attn_ms / max(n_attn, 1), 4)}
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            tf, heads_done, secs = cpu_attention_sample(seconds=args.cpu_seconds)
+            cpu = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count() or 1,
+                   "kind": "port",
+                   "sample": f"layer 0, {heads_done} head(s) x 21 query frames ({secs:.1f} s), "
+                             "traces/gen_golden.py math in numpy fp32"}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1)/sqrt(128) Q/K/V, U[0,1) tile motion)",
+            "config": {"workload": "wan21_stack_21f_30L_12H_causal", "frames": FRAMES,
+                       "tokens_per_frame": TOKENS, "layers": LAYERS, "heads": HEADS,
+                       "head_dim": HEAD_DIM, "pairs": N_PAIRS, "policy": args.policy,
+                       "set_aside_bytes": set_aside, "mask": "block-causal by frame",
+                       "flop_per_step": total_flops,
+                       "l2": "inputs 12.1 GB exceed the 126 MB L2 (no flush needed)",
+                       "parallelism": f"pairs/{world}" + (" + nccl all_gather" if world > 1 else "")},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+        if status != 0:
+            result = 3
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    return result
+
+
+def run_e2e(args, stack, scores, dev, stream, world, local_rank):
+    """Same step with Q/K/V copied from pinned host memory and O copied back,
+    per layer chunk: H2D(chunk c+1) overlaps compute(c), D2H(c) overlaps compute(c+1)."""
+    import torch
+    import torch.distributed as dist
+    h2d = torch.cuda.Stream(device=dev)
+    d2h = torch.cuda.Stream(device=dev)
+    host = []
+    for c in stack.chunks:
+        host.append(tuple(t.to("cpu").pin_memory() for t in (c.q, c.k, c.v)) +
+                    (torch.empty(c.o.shape, dtype=torch.bfloat16).pin_memory(),))
+    sp = int(stream.cuda_stream)
+    h2d_bytes = sum(sum(t.numel() * 2 for t in h[:3]) for h in host)
+    d2h_bytes = sum(h[3].numel() * 2 for h in host)
+    layer_of = {}
+    for c in stack.chunks:
+        layer_of[id(c)] = c
+
+    def step():
+        # admission + map upload for the step
+        for si, s in enumerate(stack.sessions):
+            s.plan_stack(scores)
+            if stack.persist:
+                s.upload(sp)
+        loaded = []
+        for i, c in enumerate(stack.chunks):
+            hq, hk, hv, _ = host[i]
+            with torch.cuda.stream(h2d):
+                c.k.copy_(hk, non_blocking=True)
+                c.v.copy_(hv, non_blocking=True)
+                c.q.copy_(hq, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+            loaded.append(ev)
+        for i, c in enumerate(stack.chunks):
+            stream.wait_event(loaded[i])
+            if stack.persist:
+                stack.sessions[c.session].stage_layer(c.slot, c.k.data_ptr(), c.v.data_ptr(), sp)
+            stack.attend(c, sp)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            d2h.wait_event(ev)
+            with torch.cuda.stream(d2h):
+                host[i][3].copy_(c.o, non_blocking=True)
+        if stack.persist:
+            stack.sessions[0].clear_window(sp)
+        stream.wait_stream(d2h)
+        stream.wait_stream(h2d)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n = max(1, min(args.steps, 3))
+    e0.record(stream)
+    for _ in range(n):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / n
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    return {"value": round(stack_flops() / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+            "ms_per_step": round(ms, 2), "steps": n,
+            "path": "kvp Session + kvp_attn_bf16 C ABI, pinned host Q/K/V/O per layer chunk"}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["kvp", "reference"], default="kvp")
+    ap.add_argument("--policy", default="reuse_weighted",
+                    choices=["none", "uniform", "recency", "motion", "reuse_weighted"])
+    ap.add_argument("--set-aside", type=int, default=0, help="bytes (0 = device max persisting L2)")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and "WORLD_SIZE" in os.environ:
+        world = int(os.environ["WORLD_SIZE"])
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1 and "RANK" not in os.environ:
+        print("for --gpus > 1 launch with torch.distributed.run", file=sys.stderr)
+        return 2
+    return run_kvp(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

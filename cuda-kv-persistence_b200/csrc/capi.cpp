@@ -383,6 +383,9 @@ KVP_API int kvp_session_stage(void* s, const void* const* k_layers, const void* 
                               void* stream) {
     return static_cast<kvp::Session*>(s)->stage(k_layers, v_layers, (cudaStream_t)stream);
 }
+KVP_API int kvp_session_stage_layer(void* s, int layer, const void* k, const void* v, void* stream) {
+    return static_cast<kvp::Session*>(s)->stage_layer(layer, k, v, (cudaStream_t)stream);
+}
 KVP_API int kvp_session_window(void* s, int layer, void* stream) {
     return static_cast<kvp::Session*>(s)->apply_window(layer, (cudaStream_t)stream);
 }

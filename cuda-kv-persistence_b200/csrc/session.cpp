@@ -281,6 +281,16 @@ int Session::stage(const void* const* k_layers, const void* const* v_layers, cud
     return launch_gather_rows(L, c_.layers, d_pairs_, (int)(pairs_.size() / 2), row_kv_bytes_, s);
 }
 
+int Session::stage_layer(int layer, const void* k, const void* v, cudaStream_t s) {
+    if (!d_arena_ || layer < 0 || layer >= c_.layers || !k || !v) return KVP_ERR_ARG;
+    if (pairs_.empty()) return KVP_OK;
+    GatherLayers L{};
+    L.k[0] = k;
+    L.v[0] = v;
+    L.arena[0] = arena(layer);
+    return launch_gather_rows(L, 1, d_pairs_, (int)(pairs_.size() / 2), row_kv_bytes_, s);
+}
+
 int Session::apply_window(int layer, cudaStream_t s) {
     void* a = arena(layer);
     if (!a) return KVP_ERR_ARG;

@@ -84,6 +84,8 @@ public:
     int upload(cudaStream_t s);
     // Gathers this step's rows into every layer's arena.
     int stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s);
+    // Same for one layer (used when layers' K/V arrive one at a time).
+    int stage_layer(int layer, const void* k, const void* v, cudaStream_t s);
     // Persisting window over layer's arena span (or a normal-property
     // window when this step has no span).
     int apply_window(int layer, cudaStream_t s);

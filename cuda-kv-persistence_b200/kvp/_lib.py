@@ -124,6 +124,8 @@ SIGNATURES = {
     "kvp_session_arena": (C.c_void_p, [C.c_void_p, C.c_int]),
     "kvp_session_upload": (C.c_int, [C.c_void_p, C.c_void_p]),
     "kvp_session_stage": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "kvp_session_stage_layer": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                          C.c_void_p]),
     "kvp_session_window": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
     "kvp_session_clear_window": (C.c_int, [C.c_void_p, C.c_void_p]),
 }

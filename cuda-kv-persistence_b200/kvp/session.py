@@ -114,6 +114,10 @@ class Session:
         va = (C.c_void_p * n)(*v_ptrs)
         check(self._L.kvp_session_stage(self.h, ka, va, C.c_void_p(stream)), "stage")
 
+    def stage_layer(self, layer: int, k_ptr: int, v_ptr: int, stream: int = 0):
+        check(self._L.kvp_session_stage_layer(self.h, layer, C.c_void_p(k_ptr), C.c_void_p(v_ptr),
+                                              C.c_void_p(stream)), "stage_layer")
+
     def window(self, layer: int, stream: int = 0):
         check(self._L.kvp_session_window(self.h, layer, C.c_void_p(stream)), "window")
 

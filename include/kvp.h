@@ -125,6 +125,7 @@ void* kvp_session_arena(void* s, int layer);
 int kvp_session_upload(void* s, void* stream);
 int kvp_session_stage(void* s, const void* const* k_layers, const void* const* v_layers,
                       void* stream);
+int kvp_session_stage_layer(void* s, int layer, const void* k, const void* v, void* stream);
 int kvp_session_window(void* s, int layer, void* stream);
 int kvp_session_clear_window(void* s, void* stream);
 
