@@ -198,7 +198,7 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
     info = DeviceInfo()
     lib().kvp_query_device(local_rank, C.byref(info))
     set_aside = args.set_aside or int(info.max_persisting_l2_bytes)
-    p0, p1 = pair_range(rank, world, N_PAIRS)
+    p0, p1 = pair_range(rank, world, args.pairs)
     stack = StackRank(p0=p0, p1=p1, heads=HEADS, frames=FRAMES, tokens=TOKENS,
                       policy=args.policy, set_aside=set_aside, device=dev, seed=args.seed)
     with tempfile.TemporaryDirectory() as td:
@@ -285,7 +285,7 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
         st = torch.tensor([status], device=dev, dtype=torch.int32)
         dist.all_reduce(st, op=dist.ReduceOp.MAX)
         status = int(st[0])
-    total_flops = stack_flops()
+    total_flops = stack_flops(pairs=args.pairs)
     value = total_flops / (ms / 1e3) / 1e12
 
     # ---------------- e2e through the public API with pinned host buffers
@@ -322,7 +322,7 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
             "data": "synthetic (seeded N(0,1)/sqrt(128) Q/K/V, U[0,1) tile motion)",
             "config": {"workload": "wan21_stack_21f_30L_12H_causal", "frames": FRAMES,
                        "tokens_per_frame": TOKENS, "layers": LAYERS, "heads": HEADS,
-                       "head_dim": HEAD_DIM, "pairs": N_PAIRS, "policy": args.policy,
+                       "head_dim": HEAD_DIM, "pairs": args.pairs, "policy": args.policy,
                        "set_aside_bytes": set_aside, "mask": "block-causal by frame",
                        "flop_per_step": total_flops,
                        "l2": "inputs 12.1 GB exceed the 126 MB L2 (no flush needed)",
@@ -410,7 +410,7 @@ def run_e2e(args, stack, scores, dev, stream, world, local_rank):
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
-    return {"value": round(stack_flops() / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+    return {"value": round(stack_flops(pairs=args.pairs) / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
             "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
             "ms_per_step": round(ms, 2), "steps": n,
             "path": "kvp Session + kvp_attn_bf16 C ABI, pinned host Q/K/V/O per layer chunk"}
@@ -426,6 +426,8 @@ def main() -> int:
                     choices=["none", "uniform", "recency", "motion", "reuse_weighted"])
     ap.add_argument("--set-aside", type=int, default=0, help="bytes (0 = device max persisting L2)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--pairs", type=int, default=N_PAIRS,
+                    help="(layer, head) pairs of the stack (360 = the full config; fewer only for profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

@@ -45,7 +45,7 @@ constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kDH = 128;           // head dim
 constexpr int kStages = 2;         // K|V pipeline depth
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;     // producer, MMA, 2 idle, 8 softmax warps
 constexpr uint32_t kPanel = 128 * 128;        // one [128 rows][64 bf16] swizzled panel
 constexpr uint32_t kTileBytes = 2 * kPanel;   // [128][128] bf16
 constexpr uint32_t kGroupPanel = 8 * 128;     // one 8-row group of a panel
@@ -57,12 +57,16 @@ struct __align__(1024) Smem {
     uint8_t v[kStages][kTileBytes];
     uint8_t p[kTileBytes];
     uint64_t bar_q;
-    uint64_t bar_kv_full[kStages];
-    uint64_t bar_kv_empty[kStages];
+    uint64_t bar_full[2][kStages];   // [0] = K ring, [1] = V ring
+    uint64_t bar_empty[2][kStages];
     uint64_t bar_s_full[2];
     uint64_t bar_s_free[2];
     uint64_t bar_p_full;
     uint64_t bar_pv_done;
+    uint64_t bar_red[4][2];      // row-max exchange of the two warps of a row block
+    uint64_t bar_sum[4];         // final row-sum exchange
+    float red[2][2][128];        // [tile parity][half][row] partial row max
+    float red_sum[2][128];       // [half][row] partial row sum
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -223,6 +227,12 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
     return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -287,16 +297,22 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
 
     if (threadIdx.x == 0) {
         mbar_init(&sm.bar_q, 1);
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&sm.bar_kv_full[s], 1);
-            mbar_init(&sm.bar_kv_empty[s], 1);
-        }
+        for (int op = 0; op < 2; ++op)
+            for (int s = 0; s < kStages; ++s) {
+                mbar_init(&sm.bar_full[op][s], 1);
+                mbar_init(&sm.bar_empty[op][s], 1);
+            }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sm.bar_s_full[b], 1);
-            mbar_init(&sm.bar_s_free[b], 128);
+            mbar_init(&sm.bar_s_free[b], 256);
         }
-        mbar_init(&sm.bar_p_full, 128);
+        mbar_init(&sm.bar_p_full, 256);
         mbar_init(&sm.bar_pv_done, 1);
+        for (int g = 0; g < 4; ++g) {
+            mbar_init(&sm.bar_red[g][0], 64);
+            mbar_init(&sm.bar_red[g][1], 64);
+            mbar_init(&sm.bar_sum[g], 64);
+        }
         sm.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async_smem();
@@ -313,13 +329,17 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
     const int D = P.D;
     const int hcol = w.head * kDH;
 
-    if (warp == 0) {
-        // ============================== producer ==============================
-        // Q: 8-row groups that start inside the tensor come by TMA (a group
-        // running past the end is zero-filled by TMA); groups wholly past
-        // q_rows are not loaded -- their rows only feed output rows that are
-        // never stored (S, P and O are row-independent).
-        if (lane == 0) {
+    if (warp == 0 || warp == 2) {
+        // ============================ producers ===============================
+        // Warp 0 stages Q and the K ring, warp 2 the V ring; each reads the
+        // KVMap rows of its tile itself, so K of tile j+2 can load as soon as
+        // S_j = Q K_j^T is done, independently of the slower V ring.
+        const int op = warp == 0 ? 0 : 1;
+        if (op == 0 && lane == 0) {
+            // Q: 8-row groups that start inside the tensor come by TMA (a group
+            // running past the end is zero-filled by TMA); groups wholly past
+            // q_rows are not loaded -- their rows only feed output rows that are
+            // never stored (S, P and O are row-independent).
             uint32_t qbytes = 0;
             for (int g = 0; g < kBM / 8; ++g)
                 if (w.q_row0 + 8 * g < P.q_rows) qbytes += 2 * kGroupPanel;
@@ -331,11 +351,15 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                                 (int)(w.q_row0 + 8 * g), &sm.bar_q);
             }
         }
-        int armed[kStages] = {0, 0};
+        const CUtensorMap* map128 = op == 0 ? &maps.k128 : &maps.v128;
+        const CUtensorMap* map8 = op == 0 ? &maps.k8 : &maps.v8;
+        const __nv_bfloat16* base = op == 0 ? P.k : P.v;
+        const int acol = (op == 0 ? 0 : D) + hcol;     // column of this operand in an arena row
+        int last_armed = -1;
         for (int j = 0; j < n_tiles; ++j) {
             const int s = j % kStages;
             const uint32_t ph = (uint32_t)(j / kStages) & 1u;
-            if (!warp_wait(&sm.bar_kv_empty[s], ph ^ 1u, sm, P.status)) break;
+            if (!warp_wait(&sm.bar_empty[op][s], ph ^ 1u, sm, P.status)) break;
             const long long r0 = w.klo + (long long)j * kBN;
             // Lane l classifies rows 4l..4l+3; lanes 2g, 2g+1 form 8-row group g.
             long long m[4];
@@ -348,7 +372,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 if (!pad[i] && P.kvmap) {
                     long long x = __ldg(P.kvmap + row);
                     if (x >= P.arena_rows || (x >= 0 && !P.arena)) {
-                        atomicOr(P.status, KVP_STATUS_MAP);
+                        if (op == 0) atomicOr(P.status, KVP_STATUS_MAP);
                         x = -1;
                     }
                     m[i] = x;
@@ -370,50 +394,41 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             const unsigned base_mask = __ballot_sync(0xffffffffu, g_base);
             const unsigned arena_mask = __ballot_sync(0xffffffffu, g_arena);
             const unsigned mixed_mask = ~(base_mask | arena_mask);
-            // One 128-row box per operand when no row is remapped; the box
+            // One 128-row box per panel when no row is remapped; the box
             // starts inside the tensor (r0 < khi <= kv_rows).
             const bool whole_base = __all_sync(0xffffffffu, all_neg) && P.use_tile128;
-            uint8_t* kdst = sm.k[s];
-            uint8_t* vdst = sm.v[s];
+            uint8_t* dst_tile = op == 0 ? sm.k[s] : sm.v[s];
+            uint64_t* full = &sm.bar_full[op][s];
             if (lane == 0) {
                 uint32_t bytes = 0;
                 if (whole_base) {
-                    bytes = 2 * kTileBytes;
+                    bytes = kTileBytes;
                 } else {
                     for (int g = 0; g < 16; ++g)
-                        if (((base_mask | arena_mask) >> (2 * g)) & 1u) bytes += 4 * kGroupPanel;
+                        if (((base_mask | arena_mask) >> (2 * g)) & 1u) bytes += 2 * kGroupPanel;
                 }
-                mbar_expect_tx(&sm.bar_kv_full[s], bytes);
-                if (whole_base) {
-                    for (int p = 0; p < 2; ++p) {
-                        tma_load_2d(kdst + p * kPanel, &maps.k128, hcol + 64 * p, (int)r0, &sm.bar_kv_full[s]);
-                        tma_load_2d(vdst + p * kPanel, &maps.v128, hcol + 64 * p, (int)r0, &sm.bar_kv_full[s]);
-                    }
-                }
+                mbar_expect_tx(full, bytes);
+                if (whole_base)
+                    for (int p = 0; p < 2; ++p)
+                        tma_load_2d(dst_tile + p * kPanel, map128, hcol + 64 * p, (int)r0, full);
             }
             __syncwarp();  // expect_tx is registered before any lane issues a group load
             if (!whole_base) {
-                // TMA for base / arena groups: the lane owning the group's first rows issues.
                 if (even && (g_base || g_arena)) {
                     const int g = lane >> 1;
                     for (int p = 0; p < 2; ++p) {
-                        if (g_base) {
-                            tma_load_2d(kdst + p * kPanel + g * kGroupPanel, &maps.k8, hcol + 64 * p,
-                                        (int)(r0 + 8 * g), &sm.bar_kv_full[s]);
-                            tma_load_2d(vdst + p * kPanel + g * kGroupPanel, &maps.v8, hcol + 64 * p,
-                                        (int)(r0 + 8 * g), &sm.bar_kv_full[s]);
-                        } else {
-                            tma_load_2d(kdst + p * kPanel + g * kGroupPanel, &maps.a8, hcol + 64 * p,
-                                        (int)m[0], &sm.bar_kv_full[s]);
-                            tma_load_2d(vdst + p * kPanel + g * kGroupPanel, &maps.a8, D + hcol + 64 * p,
-                                        (int)m[0], &sm.bar_kv_full[s]);
-                        }
+                        if (g_base)
+                            tma_load_2d(dst_tile + p * kPanel + g * kGroupPanel, map8, hcol + 64 * p,
+                                        (int)(r0 + 8 * g), full);
+                        else
+                            tma_load_2d(dst_tile + p * kPanel + g * kGroupPanel, &maps.a8,
+                                        acol + 64 * p, (int)m[0], full);
                     }
                 }
-                // Mixed groups: lane -> (segment = lane/8: K0,K1,V0,V1; row = lane%8),
-                // 8 chunks of 16 B per lane and row.
+                // Mixed / padding groups: lane -> (panel = lane/16, row = (lane/2)%8,
+                // chunks 4*(lane%2) .. +3); 16-byte copies into the swizzled layout.
                 unsigned mm = mixed_mask & 0x55555555u;
-                const int seg = lane >> 3, rr = lane & 7;
+                const int pnl = lane >> 4, rr = (lane >> 1) & 7, c0 = 4 * (lane & 1);
                 while (mm) {
                     const int g = __ffs(mm) >> 1;  // bit 2g set
                     mm &= mm - 1;
@@ -428,35 +443,31 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     const long long m_row = sel == 0 ? e0 : sel == 1 ? e1 : sel == 2 ? e2 : e3;
                     const long long key = r0 + row_in_tile;
                     const bool is_pad = key >= w.khi;
-                    const int pnl = seg & 1;
-                    const bool is_v = seg >= 2;
-                    const __nv_bfloat16* src;
-                    if (m_row >= 0)
-                        src = P.arena + (size_t)m_row * 2 * D + (is_v ? D : 0) + hcol + 64 * pnl;
-                    else
-                        src = (is_v ? P.v : P.k) + (size_t)key * D + hcol + 64 * pnl;
-                    uint4 buf[8];
+                    const __nv_bfloat16* src = m_row >= 0
+                        ? P.arena + (size_t)m_row * 2 * D + acol + 64 * pnl
+                        : base + (size_t)key * D + hcol + 64 * pnl;
+                    uint4 buf[4];
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        buf[c] = is_pad ? make_uint4(0, 0, 0, 0) : __ldg(reinterpret_cast<const uint4*>(src) + c);
-                    uint8_t* dst = (is_v ? vdst : kdst) + pnl * kPanel;
+                    for (int c = 0; c < 4; ++c)
+                        buf[c] = is_pad ? make_uint4(0, 0, 0, 0)
+                                        : __ldg(reinterpret_cast<const uint4*>(src) + c0 + c);
+                    uint8_t* dst = dst_tile + pnl * kPanel;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        *reinterpret_cast<uint4*>(dst + sw128_off(row_in_tile, c)) = buf[c];
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4*>(dst + sw128_off(row_in_tile, c0 + c)) = buf[c];
                 }
                 fence_proxy_async_smem();
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.bar_kv_full[s]);
-            armed[s] = j + 1;
+            if (lane == 0) mbar_arrive(full);
+            last_armed = j;
         }
         // Drain: never leave TMA writes in flight into a CTA that is exiting.
         if (lane == 0 && sm.abort_flag) {
-            for (int s = 0; s < kStages; ++s) {
-                if (!armed[s]) continue;
-                const int j = armed[s] - 1;
+            for (int j = last_armed > 0 ? last_armed - 1 : 0; j <= last_armed; ++j) {
+                if (j < 0) continue;
                 const unsigned long long t0 = globaltimer();
-                while (!mbar_try_wait(&sm.bar_kv_full[s], (uint32_t)(j / kStages) & 1u) &&
+                while (!mbar_try_wait(&sm.bar_full[op][j % kStages], (uint32_t)(j / kStages) & 1u) &&
                        globaltimer() - t0 < kWaitNs) {
                 }
             }
@@ -474,7 +485,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             for (int j = 0; ok && j <= n_tiles; ++j) {
                 if (j < n_tiles) {
                     const int s = j % kStages, b = j & 1;
-                    if (!mbar_wait(&sm.bar_kv_full[s], (uint32_t)(j / kStages) & 1u, sm, P.status)) { ok = false; break; }
+                    if (!mbar_wait(&sm.bar_full[0][s], (uint32_t)(j / kStages) & 1u, sm, P.status)) { ok = false; break; }
                     if (!mbar_wait(&sm.bar_s_free[b], ((uint32_t)(j >> 1) & 1u) ^ 1u, sm, P.status)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t k_s = smem_u32(sm.k[s]);
@@ -485,9 +496,11 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                                sw128_desc(k_s + off, 16, 1024), idS, ks > 0 ? 1u : 0u);
                     }
                     tc_commit(&sm.bar_s_full[b]);
+                    tc_commit(&sm.bar_empty[0][s]);   // K_j consumed: the K ring moves on
                 }
                 if (j >= 1) {
                     const int jp = j - 1, s = jp % kStages;
+                    if (!mbar_wait(&sm.bar_full[1][s], (uint32_t)(jp / kStages) & 1u, sm, P.status)) { ok = false; break; }
                     if (!mbar_wait(&sm.bar_p_full, (uint32_t)jp & 1u, sm, P.status)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t v_s = smem_u32(sm.v[s]);
@@ -498,7 +511,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                                sw128_desc(v_s + (uint32_t)ks * 2048, kPanel, 1024), idO,
                                (jp > 0 || ks > 0) ? 1u : 0u);
                     }
-                    tc_commit(&sm.bar_kv_empty[s]);
+                    tc_commit(&sm.bar_empty[1][s]);
                     tc_commit(&sm.bar_pv_done);
                     issued_pv = j;
                 }
@@ -514,62 +527,85 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         __syncwarp();
     } else if (warp >= 4) {
         // ========================== softmax + epilogue ========================
-        const int row = threadIdx.x - 128;            // query row in tile == TMEM lane
+        // Warps 4-11: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
+        // quarter) and key columns [64*half, 64*half+64), half = (w-4)/4, of
+        // every S tile; the two warps of a row block exchange their partial
+        // row max through shared memory once per tile (named barrier of 64).
+        const int half = (warp - 4) >> 2;
+        const int row = (warp & 3) * 32 + lane;       // query row in tile == TMEM lane
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t col0 = 64u * (uint32_t)half;
+        const int rg = warp & 3;                       // row block shared with warp w^4
         const long long my_khi = row < w.split ? w.khi_lo : w.khi;
-        float m_run = -INFINITY, l_run = 0.f;
+        const float sl2 = P.scale_log2;
+        float m_run = -INFINITY, l_run = 0.f;          // m in log2 units, scaled
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
             const int b = j & 1;
             if (!warp_wait(&sm.bar_s_full[b], (uint32_t)(j >> 1) & 1u, sm, P.status)) { ok = false; break; }
             tc_fence_after();
-            uint32_t sr[128];
-            const uint32_t s_addr = tmem + lane_base + 128 * b;
+            uint32_t sr[64];
+            const uint32_t s_addr = tmem + lane_base + 128 * b + col0;
             KVP_TMEM_LD32(s_addr + 0, (sr + 0));
             KVP_TMEM_LD32(s_addr + 32, (sr + 32));
-            KVP_TMEM_LD32(s_addr + 64, (sr + 64));
-            KVP_TMEM_LD32(s_addr + 96, (sr + 96));
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(&sm.bar_s_free[b]);
 
-            const long long key0 = w.klo + (long long)j * kBN;
-            const int valid = (int)((my_khi - key0) < kBN ? (my_khi - key0) : kBN);
-            float s[kBN];
-            float tmax = -INFINITY;
+            float s[64];
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) {
-                s[c] = c < valid ? __uint_as_float(sr[c]) * P.scale_log2 : -INFINITY;
-                tmax = fmaxf(tmax, s[c]);
+            for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sr[c]);
+            const long long key0 = w.klo + (long long)j * kBN + col0;
+            const long long left = my_khi - key0;
+            if (left < 64) {   // tail tile: keys past the row's span never count
+#pragma unroll
+                for (int c = 0; c < 64; ++c)
+                    if (c >= left) s[c] = -INFINITY;
             }
-            float m_use = m_run;
-            bool rescale = false;
-            float alpha = 1.f;
+            // row max over this half: 8 independent chains, then a short tree
+            float mx8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+            for (int c = 8; c < 64; c += 8)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(mx8[i], s[c + i]);
+            float tmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            sm.red[b][half][row] = tmax;
+            mbar_arrive(&sm.bar_red[rg][b]);
+            if (!warp_wait(&sm.bar_red[rg][b], (uint32_t)(j >> 1) & 1u, sm, P.status)) { ok = false; break; }
+            tmax = fmaxf(tmax, sm.red[b][half ^ 1][row]) * sl2;  // both halves agree on the row max
+            // Lazy rescaling: keep the running max unless it grows by > 8 (log2
+            // units), so p <= 256 and O rarely needs a TMEM round trip.
+            float m_use = m_run, alpha = 1.f;
             if (j == 0) {
                 m_use = tmax;
             } else if (tmax > m_run + 8.f) {
                 m_use = tmax;
-                alpha = exp2f(m_run - tmax);
-                rescale = true;
+                alpha = ex2_approx(m_run - tmax);
             }
-            float rsum = 0.f;
-            uint32_t pk[64];
+            const float neg_m = -m_use;
+            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < kBN; c += 2) {
-                const float p0 = exp2f(s[c] - m_use);
-                const float p1 = exp2f(s[c + 1] - m_use);
-                rsum += p0 + p1;
+            for (int c = 0; c < 64; c += 2) {
+                const float p0 = ex2_approx(fmaf(s[c], sl2, neg_m));
+                const float p1 = ex2_approx(fmaf(s[c + 1], sl2, neg_m));
+                ps[(c >> 1) & 7] += p0 + p1;
                 pk[c >> 1] = pack_bf16(p0, p1);
             }
+            const float rsum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             l_run = l_run * alpha + rsum;
             m_run = m_use;
             if (j >= 1) {
                 if (!warp_wait(&sm.bar_pv_done, (uint32_t)(j - 1) & 1u, sm, P.status)) { ok = false; break; }
                 tc_fence_after();
-                if (rescale) {
-                    const uint32_t o_addr = tmem + lane_base + 256;
+                // warp-uniform: the TMEM round trip is .sync.aligned
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                    const uint32_t o_addr = tmem + lane_base + 256 + col0;
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
+                    for (int c4 = 0; c4 < 2; ++c4) {
                         uint32_t o[32];
                         KVP_TMEM_LD32(o_addr + 32 * c4, o);
                         tmem_wait_ld();
@@ -581,27 +617,29 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     tmem_wait_st();
                 }
             }
-            // P row -> shared memory (K-major, 128B swizzle, two 64-key panels).
+            // P row half -> shared memory panel `half` (K-major, 128B swizzle).
+            uint8_t* pdst = sm.p + half * kPanel;
 #pragma unroll
-            for (int pnl = 0; pnl < 2; ++pnl)
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const int q = pnl * 32 + c * 4;
-                    *reinterpret_cast<uint4*>(sm.p + pnl * kPanel + sw128_off(row, c)) =
-                        make_uint4(pk[q], pk[q + 1], pk[q + 2], pk[q + 3]);
-                }
+            for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4*>(pdst + sw128_off(row, c)) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&sm.bar_p_full);
         }
+        // Row sum = both halves' partial sums (same running max).
+        sm.red_sum[half][row] = l_run;
+        mbar_arrive(&sm.bar_sum[rg]);
+        if (ok) ok = warp_wait(&sm.bar_sum[rg], 0, sm, P.status);
+        const float l_row = l_run + sm.red_sum[half ^ 1][row];
         if (ok && n_tiles > 0 &&
             warp_wait(&sm.bar_pv_done, (uint32_t)(n_tiles - 1) & 1u, sm, P.status)) {
             tc_fence_after();
-            const float inv = 1.f / l_run;
-            const uint32_t o_addr = tmem + lane_base + 256;
-            __nv_bfloat16* dst = P.out + (size_t)(w.q_row0 + row) * D + hcol;
+            const float inv = 1.f / l_row;
+            const uint32_t o_addr = tmem + lane_base + 256 + col0;
+            __nv_bfloat16* dst = P.out + (size_t)(w.q_row0 + row) * D + hcol + col0;
 #pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) {
+            for (int c4 = 0; c4 < 2; ++c4) {
                 uint32_t o[32];
                 KVP_TMEM_LD32(o_addr + 32 * c4, o);
                 tmem_wait_ld();
