@@ -23,7 +23,7 @@
 //               max with lazy rescaling (only when the max grows by > 8 in
 //               log2 units), P written to shared memory as bf16, then the
 //               epilogue O / l -> bf16 -> global
-// TMEM columns: S double buffer [0,256), O [256,384).  Shared memory: Q
+// TMEM columns: S ring of three 128-column accumulators [0,384), O [384,512).  Shared memory: Q
 // 32 KB, two K|V stages of 64 KB, P 32 KB.  Every mbarrier wait is bounded
 // (about one second of %globaltimer); on expiry the CTA records
 // KVP_STATUS_TIMEOUT in the status word and unwinds without hanging.
@@ -44,7 +44,8 @@ namespace {
 constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kDH = 128;           // head dim
-constexpr int kStages = 2;         // K|V pipeline depth
+constexpr int kStages = 2;         // depth of the K ring and of the V ring
+constexpr int kSBuf = 3;           // S accumulators in TMEM: S runs two tiles ahead of PV
 constexpr int kThreads = 384;     // producer, MMA, 2 idle, 8 softmax warps
 constexpr uint32_t kPanel = 128 * 128;        // one [128 rows][64 bf16] swizzled panel
 constexpr uint32_t kTileBytes = 2 * kPanel;   // [128][128] bf16
@@ -59,8 +60,8 @@ struct __align__(1024) Smem {
     uint64_t bar_q;
     uint64_t bar_full[2][kStages];   // [0] = K ring, [1] = V ring
     uint64_t bar_empty[2][kStages];
-    uint64_t bar_s_full[2];
-    uint64_t bar_s_free[2];
+    uint64_t bar_s_full[kSBuf];
+    uint64_t bar_s_free[kSBuf];
     uint64_t bar_p_full;
     uint64_t bar_pv_done;
     uint64_t bar_red[4][2];      // row-max exchange of the two warps of a row block
@@ -302,7 +303,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 mbar_init(&sm.bar_full[op][s], 1);
                 mbar_init(&sm.bar_empty[op][s], 1);
             }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kSBuf; ++b) {
             mbar_init(&sm.bar_s_full[b], 1);
             mbar_init(&sm.bar_s_free[b], 256);
         }
@@ -479,14 +480,14 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             const uint32_t p_s = smem_u32(sm.p);
             constexpr uint32_t idS = idesc_bf16(false);
             constexpr uint32_t idO = idesc_bf16(true);
-            const uint32_t tmem_o = tmem + 256;
+            const uint32_t tmem_o = tmem + 128 * kSBuf;
             bool ok = mbar_wait(&sm.bar_q, 0, sm, P.status);
             int issued_pv = 0;
-            for (int j = 0; ok && j <= n_tiles; ++j) {
+            for (int j = 0; ok && j <= n_tiles + kSBuf - 2; ++j) {
                 if (j < n_tiles) {
-                    const int s = j % kStages, b = j & 1;
+                    const int s = j % kStages, b = j % kSBuf;
                     if (!mbar_wait(&sm.bar_full[0][s], (uint32_t)(j / kStages) & 1u, sm, P.status)) { ok = false; break; }
-                    if (!mbar_wait(&sm.bar_s_free[b], ((uint32_t)(j >> 1) & 1u) ^ 1u, sm, P.status)) { ok = false; break; }
+                    if (!mbar_wait(&sm.bar_s_free[b], ((uint32_t)(j / kSBuf) & 1u) ^ 1u, sm, P.status)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t k_s = smem_u32(sm.k[s]);
 #pragma unroll
@@ -498,8 +499,8 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     tc_commit(&sm.bar_s_full[b]);
                     tc_commit(&sm.bar_empty[0][s]);   // K_j consumed: the K ring moves on
                 }
-                if (j >= 1) {
-                    const int jp = j - 1, s = jp % kStages;
+                if (j >= kSBuf - 1 && j - (kSBuf - 1) < n_tiles) {
+                    const int jp = j - (kSBuf - 1), s = jp % kStages;
                     if (!mbar_wait(&sm.bar_full[1][s], (uint32_t)(jp / kStages) & 1u, sm, P.status)) { ok = false; break; }
                     if (!mbar_wait(&sm.bar_p_full, (uint32_t)jp & 1u, sm, P.status)) { ok = false; break; }
                     tc_fence_after();
@@ -513,7 +514,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     }
                     tc_commit(&sm.bar_empty[1][s]);
                     tc_commit(&sm.bar_pv_done);
-                    issued_pv = j;
+                    issued_pv = jp + 1;
                 }
             }
             // Drain: the last committed PV must land before TMEM is freed.
@@ -541,16 +542,17 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         float m_run = -INFINITY, l_run = 0.f;          // m in log2 units, scaled
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            const int b = j & 1;
-            if (!warp_wait(&sm.bar_s_full[b], (uint32_t)(j >> 1) & 1u, sm, P.status)) { ok = false; break; }
+            const int b = j & 1;           // parity buffer of the row-max exchange
+            const int sb = j % kSBuf;      // S accumulator of this tile
+            if (!warp_wait(&sm.bar_s_full[sb], (uint32_t)(j / kSBuf) & 1u, sm, P.status)) { ok = false; break; }
             tc_fence_after();
             uint32_t sr[64];
-            const uint32_t s_addr = tmem + lane_base + 128 * b + col0;
+            const uint32_t s_addr = tmem + lane_base + 128 * sb + col0;
             KVP_TMEM_LD32(s_addr + 0, (sr + 0));
             KVP_TMEM_LD32(s_addr + 32, (sr + 32));
             tmem_wait_ld();
             tc_fence_before();
-            mbar_arrive(&sm.bar_s_free[b]);
+            mbar_arrive(&sm.bar_s_free[sb]);
 
             float s[64];
 #pragma unroll
@@ -603,7 +605,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 tc_fence_after();
                 // warp-uniform: the TMEM round trip is .sync.aligned
                 if (__any_sync(0xffffffffu, alpha != 1.f)) {
-                    const uint32_t o_addr = tmem + lane_base + 256 + col0;
+                    const uint32_t o_addr = tmem + lane_base + 128 * kSBuf + col0;
 #pragma unroll
                     for (int c4 = 0; c4 < 2; ++c4) {
                         uint32_t o[32];
@@ -636,7 +638,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             warp_wait(&sm.bar_pv_done, (uint32_t)(n_tiles - 1) & 1u, sm, P.status)) {
             tc_fence_after();
             const float inv = 1.f / l_row;
-            const uint32_t o_addr = tmem + lane_base + 256 + col0;
+            const uint32_t o_addr = tmem + lane_base + 128 * kSBuf + col0;
             __nv_bfloat16* dst = P.out + (size_t)(w.q_row0 + row) * D + hcol + col0;
 #pragma unroll
             for (int c4 = 0; c4 < 2; ++c4) {
