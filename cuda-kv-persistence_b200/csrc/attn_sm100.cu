@@ -357,26 +357,33 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         const __nv_bfloat16* base = op == 0 ? P.k : P.v;
         const int acol = (op == 0 ? 0 : D) + hcol;     // column of this operand in an arena row
         int last_armed = -1;
+        // KVMap rows of a tile are read one tile ahead, so their L2 latency
+        // overlaps the wait for a free stage instead of delaying the TMA issue.
+        auto map_rows = [&](int jj, long long (&mm)[4]) {
+            const long long rr0 = w.klo + (long long)jj * kBN;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const long long row = rr0 + 4 * lane + i;
+                mm[i] = (jj < n_tiles && row < w.khi && P.kvmap) ? __ldg(P.kvmap + row) : -1;
+            }
+        };
+        long long m_next[4];
+        map_rows(0, m_next);
         for (int j = 0; j < n_tiles; ++j) {
+            long long m[4] = {m_next[0], m_next[1], m_next[2], m_next[3]};
+            map_rows(j + 1, m_next);
             const int s = j % kStages;
             const uint32_t ph = (uint32_t)(j / kStages) & 1u;
             if (!warp_wait(&sm.bar_empty[op][s], ph ^ 1u, sm, P.status)) break;
             const long long r0 = w.klo + (long long)j * kBN;
             // Lane l classifies rows 4l..4l+3; lanes 2g, 2g+1 form 8-row group g.
-            long long m[4];
             bool pad[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const long long row = r0 + 4 * lane + i;
-                pad[i] = row >= w.khi;
-                m[i] = -1;
-                if (!pad[i] && P.kvmap) {
-                    long long x = __ldg(P.kvmap + row);
-                    if (x >= P.arena_rows || (x >= 0 && !P.arena)) {
-                        if (op == 0) atomicOr(P.status, KVP_STATUS_MAP);
-                        x = -1;
-                    }
-                    m[i] = x;
+                pad[i] = r0 + 4 * lane + i >= w.khi;
+                if (m[i] >= P.arena_rows || (m[i] >= 0 && !P.arena)) {
+                    if (op == 0) atomicOr(P.status, KVP_STATUS_MAP);
+                    m[i] = -1;   // out-of-range entry: read the base row
                 }
             }
             const bool all_neg = m[0] < 0 && m[1] < 0 && m[2] < 0 && m[3] < 0;
