@@ -91,6 +91,23 @@ typedef struct {
 
 int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
 
+/* No counterpart in the reference.  kvp_attn_bf16 for callers that cannot
+ * allocate device memory -- code inside a stream capture, hosts whose
+ * allocator owns all device memory, serving loops that cannot take a
+ * first-call cudaMalloc.  Nothing is allocated: the status word and a device
+ * copy of the KVMap, which the caller passes in HOST memory (host_kvmap,
+ * int64, (q_frame0+frames)*tokens rows, at most 65,536; NULL = no remap;
+ * io->kvmap must be NULL), live in a static device array of ~512 KB that
+ * each GPU holds until exit.  Q/K/V/Out/arena are still device memory from
+ * the caller.  The first call on a device looks the array up (make it before
+ * any stream capture); all calls share the array (the status word is reset
+ * per call), so calls that overlap on the GPU race.  host_status (may be
+ * NULL) receives the status word and then the call synchronises `stream`.
+ * Queued kvtm_* staging copies are not flushed: call kvtm_flush first.
+ * Returns -3 when the map exceeds the limit. */
+int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d,
+                          const long long* host_kvmap, int* host_status, void* stream);
+
 /* ---- Session: the per-frame admission loop / KVMap emitter of
  * src/run_policy_experiment.cu:156-274 as a library. */
 typedef struct {
