@@ -288,6 +288,17 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
     total_flops = stack_flops(pairs=args.pairs)
     value = total_flops / (ms / 1e3) / 1e12
 
+    gather_check = None
+    if world > 1:
+        # The last step's gather must hold every rank's outputs: compare each
+        # rank's own checksum with the checksum of its segment on rank 0.
+        last = flat[(args.warmup + args.steps - 1) & 1]
+        mine = torch.tensor([last.double().sum().item()], device=dev, dtype=torch.float64)
+        sums = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(sums, mine)
+        seg = gathered.view(world, -1).double().sum(dim=1)
+        gather_check = bool(torch.allclose(seg, torch.cat(sums), rtol=0, atol=0))
+
     # ---------------- e2e through the public API with pinned host buffers
     e2e = None
     if not args.no_e2e:
@@ -333,6 +344,7 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "device_status": status,
+            "gather_check": gather_check,
         }
         print(json.dumps(line), flush=True)
         if status != 0:

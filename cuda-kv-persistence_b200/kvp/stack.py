@@ -18,6 +18,7 @@ import torch
 
 from .attention import attn_bf16
 from .session import Session
+from .shard import chunks_of, pair_range  # noqa: F401  (pair_range re-exported)
 
 HEAD_DIM = 128
 
@@ -33,25 +34,6 @@ class Chunk:
     o: torch.Tensor
     session: int = 0    # index into StackRank.sessions
     slot: int = 0       # arena index within that session
-
-
-def pair_range(rank: int, world: int, n_pairs: int):
-    """Contiguous block of pairs for `rank` (sizes differ by at most one)."""
-    base, extra = divmod(n_pairs, world)
-    p0 = rank * base + min(rank, extra)
-    return p0, p0 + base + (1 if rank < extra else 0)
-
-
-def chunks_of(p0: int, p1: int, heads: int):
-    """[(layer, head0, nheads)] covering pairs [p0, p1)."""
-    out = []
-    p = p0
-    while p < p1:
-        layer, h = divmod(p, heads)
-        n = min(heads - h, p1 - p)
-        out.append((layer, h, n))
-        p += n
-    return out
 
 
 def pair_qkv(layer: int, head: int, rows: int, seed: int, device, heads: int) -> tuple:
