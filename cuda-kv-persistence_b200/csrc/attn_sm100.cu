@@ -796,3 +796,38 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
 }
 
 }  // namespace kvp
+
+// ------------------------------------------------------- bounded-wait probe
+// Exercises the timeout path of the bounded mbarrier waits without hanging
+// anything: the barrier expects two arrivals and only one ever comes, so the
+// wait runs out after limit_ns and the kernel records KVP_STATUS_TIMEOUT.
+namespace kvp {
+namespace {
+__global__ void bounded_wait_probe_kernel(int* status, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 2);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_arrive(&bar);
+        const unsigned long long t0 = globaltimer();
+        bool done = false;
+        while (!(done = mbar_try_wait(&bar, 0)))
+            if (globaltimer() - t0 > limit_ns) break;
+        if (!done) atomicOr(status, KVP_STATUS_TIMEOUT);
+    }
+}
+}  // namespace
+
+int launch_bounded_wait_probe(long long limit_ns, int* d_status, cudaStream_t stream) {
+    if (limit_ns <= 0 || limit_ns > 5000000000LL || !d_status) {
+        set_error("probe: limit must be in (0, 5 s]");
+        return KVP_ERR_ARG;
+    }
+    bounded_wait_probe_kernel<<<1, 32, 0, stream>>>(d_status, (unsigned long long)limit_ns);
+    KVP_CUDA(cudaGetLastError());
+    return KVP_OK;
+}
+}  // namespace kvp

@@ -46,4 +46,8 @@ struct AttnDesc {
 
 int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream);
 
+// A kernel whose bounded mbarrier wait cannot complete: records
+// KVP_STATUS_TIMEOUT after limit_ns (<= 5 s).  For tests of the timeout path.
+int launch_bounded_wait_probe(long long limit_ns, int* d_status, cudaStream_t stream);
+
 }  // namespace kvp

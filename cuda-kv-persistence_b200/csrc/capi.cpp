@@ -413,6 +413,12 @@ struct kvp_attn_desc {
     int tokens, frames, q_frame0, mode, window, heads, head_dim, head0, nheads, flat;
 };
 
+KVP_API int kvp_probe_bounded_wait(long long limit_ns, void* stream) {
+    int* st = kvp::status_word();
+    if (!st) return kvp::KVP_ERR_CUDA;
+    return kvp::launch_bounded_wait_probe(limit_ns, st, (cudaStream_t)stream);
+}
+
 KVP_API int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream) {
     if (!io || !d) return kvp::KVP_ERR_ARG;
     int rc = kvp::flush_all_managers();

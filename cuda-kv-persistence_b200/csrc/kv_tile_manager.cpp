@@ -287,7 +287,23 @@ void KVTileManager::streaming_end() {
 // ---- batched staging copies -----------------------------------------------
 
 void KVTileManager::queue_copy(void* dst, const void* src, size_t bytes) {
+    // One flush runs its copies in parallel, while the reference's
+    // cudaMemcpyAsync calls ran in stream order.  A later copy to the same
+    // destination therefore replaces the queued one (the later write wins,
+    // as in stream order); a partial overlap with a queued destination
+    // issues the queue first.
     if (dry_run() || bytes == 0) return;
+    const uintptr_t d0 = (uintptr_t)dst, d1 = d0 + bytes;
+    for (CopyOp& op : pending_) {
+        const uintptr_t o0 = (uintptr_t)op.dst, o1 = o0 + op.bytes;
+        if (d1 <= o0 || o1 <= d0) continue;
+        if (o0 == d0 && op.bytes == bytes) {
+            op.src = src;
+            return;
+        }
+        flush();
+        break;
+    }
     pending_.push_back({src, dst, (uint64_t)bytes});
 }
 

@@ -99,6 +99,7 @@ SIGNATURES = {
     "kvp_version": (C.c_char_p, []),
     "kvp_last_error": (C.c_char_p, []),
     "kvp_read_status": (C.c_int, [C.c_void_p]),
+    "kvp_probe_bounded_wait": (C.c_int, [C.c_longlong, C.c_void_p]),
     "kvp_query_device": (C.c_int, [C.c_int, C.POINTER(DeviceInfo)]),
     "tgp_select": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                              C.c_void_p, c_int_p]),

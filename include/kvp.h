@@ -22,6 +22,12 @@ const char* kvp_last_error(void);
  * device wait expired.  Synchronises `stream`, returns and clears it. */
 int kvp_read_status(void* stream);
 
+/* Diagnostics: launches one kernel whose bounded mbarrier wait can never
+ * complete (0 < limit_ns <= 5 s); it gives up after limit_ns and sets status
+ * bit 1, exactly as an expired wait in the attention kernel does.  Lets tests
+ * exercise failure detection without hanging a GPU. */
+int kvp_probe_bounded_wait(long long limit_ns, void* stream);
+
 typedef struct {
     int device, sm_count, cc_major, cc_minor;
     long long l2_bytes;
