@@ -200,7 +200,8 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
     set_aside = args.set_aside or int(info.max_persisting_l2_bytes)
     p0, p1 = pair_range(rank, world, args.pairs)
     stack = StackRank(p0=p0, p1=p1, heads=HEADS, frames=FRAMES, tokens=TOKENS,
-                      policy=args.policy, set_aside=set_aside, device=dev, seed=args.seed)
+                      policy=args.policy, set_aside=set_aside, device=dev, seed=args.seed,
+                      window=args.window == "on")
     with tempfile.TemporaryDirectory() as td:
         scores = traces.csv_round_trip(traces.motion_config4(frames=FRAMES, seed=args.seed), td)
     stream = torch.cuda.Stream(device=dev)
@@ -240,7 +241,7 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
                 if timed:
                     e1.record(stream)
                     attn_events.append((e0, e1))
-            if stack.persist:
+            if stack.persist and stack.use_window:
                 stack.sessions[0].clear_window(sp)
         if world > 1:
             ev = torch.cuda.Event()
@@ -334,7 +335,8 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
             "config": {"workload": "wan21_stack_21f_30L_12H_causal", "frames": FRAMES,
                        "tokens_per_frame": TOKENS, "layers": LAYERS, "heads": HEADS,
                        "head_dim": HEAD_DIM, "pairs": args.pairs, "policy": args.policy,
-                       "set_aside_bytes": set_aside, "mask": "block-causal by frame",
+                       "set_aside_bytes": set_aside, "persisting_window": args.window,
+                       "mask": "block-causal by frame",
                        "flop_per_step": total_flops,
                        "l2": "inputs 12.1 GB exceed the 126 MB L2 (no flush needed)",
                        "parallelism": f"pairs/{world}" + (" + nccl all_gather" if world > 1 else "")},
@@ -399,7 +401,7 @@ def run_e2e(args, stack, scores, dev, stream, world, local_rank):
             d2h.wait_event(ev)
             with torch.cuda.stream(d2h):
                 host[i][3].copy_(c.o, non_blocking=True)
-        if stack.persist:
+        if stack.persist and stack.use_window:
             stack.sessions[0].clear_window(sp)
         stream.wait_stream(d2h)
         stream.wait_stream(h2d)
@@ -437,6 +439,8 @@ def main() -> int:
     ap.add_argument("--policy", default="reuse_weighted",
                     choices=["none", "uniform", "recency", "motion", "reuse_weighted"])
     ap.add_argument("--set-aside", type=int, default=0, help="bytes (0 = device max persisting L2)")
+    ap.add_argument("--window", choices=["on", "off"], default="on",
+                    help="persisting access-policy window over each layer's arena")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--pairs", type=int, default=N_PAIRS,
                     help="(layer, head) pairs of the stack (360 = the full config; fewer only for profiling)")

@@ -56,29 +56,27 @@ struct __align__(1024) Smem {
     uint8_t q[kTileBytes];
     uint8_t k[kStages][kTileBytes];
     uint8_t v[kStages][kTileBytes];
-    uint8_t p[kTileBytes];
+    uint8_t p[2][kTileBytes];       // P double buffer: tile j uses p[j & 1]
     uint64_t bar_q;
     uint64_t bar_full[2][kStages];   // [0] = K ring, [1] = V ring
     uint64_t bar_empty[2][kStages];
     uint64_t bar_s_full[kSBuf];
     uint64_t bar_s_free[kSBuf];
-    uint64_t bar_p_full;
-    uint64_t bar_pv_done;
+    uint64_t bar_p_full[2];         // P_j written into p[j & 1]
+    uint64_t bar_pv_done[2];        // PV_j done -> p[j & 1] free (one barrier per buffer)
     uint64_t bar_red[4][2];      // row-max exchange of the two warps of a row block
     uint64_t bar_sum[4];         // final row-sum exchange
     float red[2][2][128];        // [tile parity][half][row] partial row max
-    float red_sum[2][128];       // [half][row] partial row sum
     uint32_t tmem_base;
     int abort_flag;
 };
 
+constexpr int kBoxKinds = 5;       // TMA box heights 8, 16, 32, 64, 128 rows
+
 struct TmaMaps {
-    CUtensorMap q8;     // Q   [q_rows][D], box 64 x 8
-    CUtensorMap k8;     // K   [kv_rows][D], box 64 x 8
-    CUtensorMap v8;
-    CUtensorMap k128;   // K   [kv_rows][D], box 64 x 128
-    CUtensorMap v128;
-    CUtensorMap a8;     // arena [arena_rows][2D], box 64 x 8
+    CUtensorMap q8;                 // Q [q_rows][D], box 64 x 8
+    CUtensorMap kv[2][kBoxKinds];   // K / V [kv_rows][D], box 64 x (8 << i)
+    CUtensorMap a[kBoxKinds];       // arena [arena_rows][2D], box 64 x (8 << i)
 };
 
 struct Params {
@@ -90,7 +88,7 @@ struct Params {
     int* status;
     long long q_rows, kv_rows, arena_rows;
     int D, T, frames, q_frame0, mode, window, head0, nheads, flat, items_per_head, n_qt;
-    int use_tile128, arena_tma;
+    int base_boxes, arena_boxes;   // box kinds usable (heights <= tensor rows); 0 = no arena TMA
     float scale_log2;
 };
 
@@ -234,6 +232,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
+// 2^x on the FMA/ALU pipes: x = n + f with n = round(x) and f in [-1/2, 1/2],
+// 2^f by a cubic fitted here by iteratively reweighted least squares on the
+// relative error (max relative error 1.4e-4 over x in [-126, 8], against bf16's
+// 3.9e-3 rounding of P), 2^n added to the exponent bits.  Inputs below -126
+// are clamped to -126 (the result stays a positive number below 2^-125,
+// which is 0 in the bf16 P and negligible in the row sum; -inf lands there too).
+__device__ __forceinline__ float ex2_poly(float x) {
+    x = fmaxf(x, -126.f);
+    const float t = x + 12582912.f;           // 1.5 * 2^23: round to nearest integer
+    const float f = x - (t - 12582912.f);
+    float p = fmaf(5.517162719e-02f, f, 2.426111432e-01f);
+    p = fmaf(p, f, 6.932609953e-01f);
+    p = fmaf(p, f, 9.999280725e-01f);
+    const int n = __float_as_int(t) - 0x4B400000;
+    return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -290,7 +305,13 @@ __device__ __forceinline__ Work decode_work(const Params& P) {
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_constant__ Params P) {
     extern __shared__ uint8_t smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // The layout needs a 1024-byte aligned base (128B-swizzle atoms) and uses
+    // the whole 227 KB, so there is no room to realign: refuse instead.
+    if (reinterpret_cast<uintptr_t>(smem_raw) & 1023) {
+        if (threadIdx.x == 0) atomicOr(P.status, KVP_STATUS_ALIGN);
+        return;
+    }
+    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const Work w = decode_work(P);
@@ -307,8 +328,10 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             mbar_init(&sm.bar_s_full[b], 1);
             mbar_init(&sm.bar_s_free[b], 256);
         }
-        mbar_init(&sm.bar_p_full, 256);
-        mbar_init(&sm.bar_pv_done, 1);
+        mbar_init(&sm.bar_p_full[0], 256);
+        mbar_init(&sm.bar_p_full[1], 256);
+        mbar_init(&sm.bar_pv_done[0], 1);
+        mbar_init(&sm.bar_pv_done[1], 1);
         for (int g = 0; g < 4; ++g) {
             mbar_init(&sm.bar_red[g][0], 64);
             mbar_init(&sm.bar_red[g][1], 64);
@@ -352,8 +375,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                                 (int)(w.q_row0 + 8 * g), &sm.bar_q);
             }
         }
-        const CUtensorMap* map128 = op == 0 ? &maps.k128 : &maps.v128;
-        const CUtensorMap* map8 = op == 0 ? &maps.k8 : &maps.v8;
+        const CUtensorMap* base_maps = maps.kv[op];
         const __nv_bfloat16* base = op == 0 ? P.k : P.v;
         const int acol = (op == 0 ? 0 : D) + hcol;     // column of this operand in an arena row
         int last_armed = -1;
@@ -398,13 +420,21 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             const bool p_pad0 = __shfl_xor_sync(0xffffffffu, pad[0], 1);
             const bool group_pad = even ? pad[0] : p_pad0;
             const bool g_base = all_neg && p_neg && !group_pad;
-            const bool g_arena = P.arena_tma && asc && p_asc && (even ? p_m0 == m[0] + 4 : m[0] == p_m0 + 4);
+            const bool g_arena = P.arena_boxes > 0 && asc && p_asc && (even ? p_m0 == m[0] + 4 : m[0] == p_m0 + 4);
             const unsigned base_mask = __ballot_sync(0xffffffffu, g_base);
             const unsigned arena_mask = __ballot_sync(0xffffffffu, g_arena);
             const unsigned mixed_mask = ~(base_mask | arena_mask);
             // One 128-row box per panel when no row is remapped; the box
             // starts inside the tensor (r0 < khi <= kv_rows).
-            const bool whole_base = __all_sync(0xffffffffu, all_neg) && P.use_tile128;
+            const bool whole_base = __all_sync(0xffffffffu, all_neg) && P.base_boxes == kBoxKinds;
+            // Runs: a base or arena group continues the previous group's run
+            // when it is the same kind and, for arena groups, its slots follow
+            // on; each run head issues power-of-two boxes for the whole run.
+            const long long prev_m0 = __shfl_up_sync(0xffffffffu, m[0], 2);
+            const bool cont = even && lane >= 2 &&
+                ((g_base && ((base_mask >> (lane - 2)) & 1u)) ||
+                 (g_arena && ((arena_mask >> (lane - 2)) & 1u) && m[0] == prev_m0 + 8));
+            const unsigned cont_mask = __ballot_sync(0xffffffffu, cont);
             uint8_t* dst_tile = op == 0 ? sm.k[s] : sm.v[s];
             uint64_t* full = &sm.bar_full[op][s];
             if (lane == 0) {
@@ -418,19 +448,26 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 mbar_expect_tx(full, bytes);
                 if (whole_base)
                     for (int p = 0; p < 2; ++p)
-                        tma_load_2d(dst_tile + p * kPanel, map128, hcol + 64 * p, (int)r0, full);
+                        tma_load_2d(dst_tile + p * kPanel, &base_maps[kBoxKinds - 1], hcol + 64 * p,
+                                    (int)r0, full);
             }
             __syncwarp();  // expect_tx is registered before any lane issues a group load
             if (!whole_base) {
-                if (even && (g_base || g_arena)) {
+                if (even && (g_base || g_arena) && !cont) {
                     const int g = lane >> 1;
-                    for (int p = 0; p < 2; ++p) {
-                        if (g_base)
-                            tma_load_2d(dst_tile + p * kPanel + g * kGroupPanel, map8, hcol + 64 * p,
-                                        (int)(r0 + 8 * g), full);
-                        else
-                            tma_load_2d(dst_tile + p * kPanel + g * kGroupPanel, &maps.a8,
-                                        acol + 64 * p, (int)m[0], full);
+                    int len = 1;                         // groups in this run
+                    while (g + len < 16 && ((cont_mask >> (2 * (g + len))) & 1u)) ++len;
+                    const CUtensorMap* mp = g_base ? base_maps : maps.a;
+                    const int kinds = g_base ? P.base_boxes : P.arena_boxes;
+                    for (int off = 0; off < len;) {
+                        int kind = 0;                    // largest box that fits the rest of the run
+                        while (kind + 1 < kinds && (2 << kind) <= len - off) ++kind;
+                        const int row = g_base ? (int)(r0 + 8 * (g + off)) : (int)(m[0] + 8 * off);
+                        const int col = g_base ? hcol : acol;
+                        for (int p = 0; p < 2; ++p)
+                            tma_load_2d(dst_tile + p * kPanel + (g + off) * kGroupPanel, &mp[kind],
+                                        col + 64 * p, row, full);
+                        off += 1 << kind;
                     }
                 }
                 // Mixed / padding groups: lane -> (panel = lane/16, row = (lane/2)%8,
@@ -464,7 +501,9 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     for (int c = 0; c < 4; ++c)
                         *reinterpret_cast<uint4*>(dst + sw128_off(row_in_tile, c0 + c)) = buf[c];
                 }
-                fence_proxy_async_smem();
+                // make the warp's own stores visible to the tensor cores (only
+                // when some group was copied by hand)
+                if (mixed_mask & 0x55555555u) fence_proxy_async_smem();
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(full);
@@ -484,7 +523,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         // ============================ MMA issuer ==============================
         if (lane == 0) {
             const uint32_t q_s = smem_u32(sm.q);
-            const uint32_t p_s = smem_u32(sm.p);
+            const uint32_t p_s0 = smem_u32(sm.p[0]);
             constexpr uint32_t idS = idesc_bf16(false);
             constexpr uint32_t idO = idesc_bf16(true);
             const uint32_t tmem_o = tmem + 128 * kSBuf;
@@ -509,25 +548,26 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 if (j >= kSBuf - 1 && j - (kSBuf - 1) < n_tiles) {
                     const int jp = j - (kSBuf - 1), s = jp % kStages;
                     if (!mbar_wait(&sm.bar_full[1][s], (uint32_t)(jp / kStages) & 1u, sm, P.status)) { ok = false; break; }
-                    if (!mbar_wait(&sm.bar_p_full, (uint32_t)jp & 1u, sm, P.status)) { ok = false; break; }
+                    if (!mbar_wait(&sm.bar_p_full[jp & 1], (uint32_t)(jp >> 1) & 1u, sm, P.status)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t v_s = smem_u32(sm.v[s]);
 #pragma unroll
                     for (int ks = 0; ks < kBN / 16; ++ks) {
                         const uint32_t a_off = (uint32_t)(ks >> 2) * kPanel + (uint32_t)(ks & 3) * 32;
-                        tc_mma(tmem_o, sw128_desc(p_s + a_off, 16, 1024),
+                        tc_mma(tmem_o, sw128_desc(p_s0 + (uint32_t)(jp & 1) * kTileBytes + a_off, 16, 1024),
                                sw128_desc(v_s + (uint32_t)ks * 2048, kPanel, 1024), idO,
                                (jp > 0 || ks > 0) ? 1u : 0u);
                     }
                     tc_commit(&sm.bar_empty[1][s]);
-                    tc_commit(&sm.bar_pv_done);
+                    tc_commit(&sm.bar_pv_done[jp & 1]);
                     issued_pv = jp + 1;
                 }
             }
             // Drain: the last committed PV must land before TMEM is freed.
             if (issued_pv > 0) {
                 const unsigned long long t0 = globaltimer();
-                while (!mbar_try_wait(&sm.bar_pv_done, (uint32_t)(issued_pv - 1) & 1u) &&
+                const int last = issued_pv - 1;
+                while (!mbar_try_wait(&sm.bar_pv_done[last & 1], (uint32_t)(last >> 1) & 1u) &&
                        globaltimer() - t0 < kWaitNs) {
                 }
             }
@@ -579,70 +619,89 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             for (int c = 8; c < 64; c += 8)
 #pragma unroll
                 for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(mx8[i], s[c + i]);
-            float tmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            sm.red[b][half][row] = tmax;
+            const float half_max = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                         fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            sm.red[b][half][row] = half_max;
             mbar_arrive(&sm.bar_red[rg][b]);
+            // Lazy rescaling: keep the running max unless the row max grows by
+            // more than 8 (log2 units), so p <= 256 and O rarely needs a TMEM
+            // round trip.  After the first tile the exponentials are computed
+            // with the running max while the partner half's max is still in
+            // flight; only a row whose max jumps recomputes them.
+            float ps[8];
+            uint32_t pk[32];
+            auto exp_half = [&](float m) {
+                const float neg_m = -m;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+#pragma unroll
+                for (int c = 0; c < 64; c += 2) {
+                    const float x0 = fmaf(s[c], sl2, neg_m);
+                    const float x1 = fmaf(s[c + 1], sl2, neg_m);
+                    // a quarter of the exponentials run on the FMA pipe
+                    const bool fma_pipe = (c & 7) == 6;
+                    const float p0 = fma_pipe ? ex2_poly(x0) : ex2_approx(x0);
+                    const float p1 = fma_pipe ? ex2_poly(x1) : ex2_approx(x1);
+                    ps[(c >> 1) & 7] += p0 + p1;
+                    pk[c >> 1] = pack_bf16(p0, p1);
+                }
+            };
+            if (j > 0) exp_half(m_run);
             if (!warp_wait(&sm.bar_red[rg][b], (uint32_t)(j >> 1) & 1u, sm, P.status)) { ok = false; break; }
-            tmax = fmaxf(tmax, sm.red[b][half ^ 1][row]) * sl2;  // both halves agree on the row max
-            // Lazy rescaling: keep the running max unless it grows by > 8 (log2
-            // units), so p <= 256 and O rarely needs a TMEM round trip.
+            const float tmax = fmaxf(half_max, sm.red[b][half ^ 1][row]) * sl2;  // both halves agree
             float m_use = m_run, alpha = 1.f;
             if (j == 0) {
                 m_use = tmax;
+                exp_half(m_use);
             } else if (tmax > m_run + 8.f) {
                 m_use = tmax;
                 alpha = ex2_approx(m_run - tmax);
-            }
-            const float neg_m = -m_use;
-            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            uint32_t pk[32];
-#pragma unroll
-            for (int c = 0; c < 64; c += 2) {
-                const float p0 = ex2_approx(fmaf(s[c], sl2, neg_m));
-                const float p1 = ex2_approx(fmaf(s[c + 1], sl2, neg_m));
-                ps[(c >> 1) & 7] += p0 + p1;
-                pk[c >> 1] = pack_bf16(p0, p1);
+                exp_half(m_use);
             }
             const float rsum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
             l_run = l_run * alpha + rsum;
             m_run = m_use;
-            if (j >= 1) {
-                if (!warp_wait(&sm.bar_pv_done, (uint32_t)(j - 1) & 1u, sm, P.status)) { ok = false; break; }
+            // warp-uniform: the TMEM round trip is .sync.aligned
+            const bool any_rescale = __any_sync(0xffffffffu, alpha != 1.f);
+            if (j >= 1 && any_rescale) {
+                // O is rescaled only once PV_{j-1} has finished accumulating
+                if (!warp_wait(&sm.bar_pv_done[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, sm, P.status)) { ok = false; break; }
                 tc_fence_after();
-                // warp-uniform: the TMEM round trip is .sync.aligned
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
-                    const uint32_t o_addr = tmem + lane_base + 128 * kSBuf + col0;
+                const uint32_t o_addr = tmem + lane_base + 128 * kSBuf + col0;
 #pragma unroll
-                    for (int c4 = 0; c4 < 2; ++c4) {
-                        uint32_t o[32];
-                        KVP_TMEM_LD32(o_addr + 32 * c4, o);
-                        tmem_wait_ld();
+                for (int c4 = 0; c4 < 2; ++c4) {
+                    uint32_t o[32];
+                    KVP_TMEM_LD32(o_addr + 32 * c4, o);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 32; ++c)
-                            o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                        KVP_TMEM_ST32(o_addr + 32 * c4, o);
-                    }
-                    tmem_wait_st();
+                    for (int c = 0; c < 32; ++c)
+                        o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                    KVP_TMEM_ST32(o_addr + 32 * c4, o);
                 }
+                tmem_wait_st();
+            } else if (j >= 2) {
+                // P buffer j&1 was last read by PV_{j-2}
+                if (!warp_wait(&sm.bar_pv_done[j & 1], (uint32_t)((j - 2) >> 1) & 1u, sm, P.status)) { ok = false; break; }
             }
-            // P row half -> shared memory panel `half` (K-major, 128B swizzle).
-            uint8_t* pdst = sm.p + half * kPanel;
+            // P row half -> shared memory panel `half` of buffer j&1 (K-major, 128B swizzle).
+            uint8_t* pdst = sm.p[j & 1] + half * kPanel;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 *reinterpret_cast<uint4*>(pdst + sw128_off(row, c)) =
                     make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(&sm.bar_p_full);
+            mbar_arrive(&sm.bar_p_full[j & 1]);
         }
         // Row sum = both halves' partial sums (same running max).
-        sm.red_sum[half][row] = l_run;
+        // (the max buffer of parity n_tiles&1 was last read two tiles ago)
+        float (&red_sum)[2][128] = sm.red[n_tiles & 1];
+        red_sum[half][row] = l_run;
         mbar_arrive(&sm.bar_sum[rg]);
         if (ok) ok = warp_wait(&sm.bar_sum[rg], 0, sm, P.status);
-        const float l_row = l_run + sm.red_sum[half ^ 1][row];
+        const float l_row = l_run + red_sum[half ^ 1][row];
         if (ok && n_tiles > 0 &&
-            warp_wait(&sm.bar_pv_done, (uint32_t)(n_tiles - 1) & 1u, sm, P.status)) {
+            warp_wait(&sm.bar_pv_done[(n_tiles - 1) & 1], (uint32_t)((n_tiles - 1) >> 1) & 1u, sm, P.status)) {
             tc_fence_after();
             const float inv = 1.f / l_row;
             const uint32_t o_addr = tmem + lane_base + 128 * kSBuf + col0;
@@ -744,16 +803,25 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
     }
     TmaMaps maps;
     std::memset(&maps, 0, sizeof maps);
+    // Box kinds whose height fits the tensor (a box never starts past the
+    // end, and a taller box than the tensor is never encoded).
+    int base_boxes = 0, arena_boxes = 0;
+    while (base_boxes < kBoxKinds && (8LL << base_boxes) <= io.kv_rows) ++base_boxes;
+    if (io.arena)
+        while (arena_boxes < kBoxKinds && (8LL << arena_boxes) <= io.arena_rows) ++arena_boxes;
     int rc = make_map(&maps.q8, io.q, io.q_rows, D, D, 8);
-    if (!rc) rc = make_map(&maps.k8, io.k, io.kv_rows, D, D, 8);
-    if (!rc) rc = make_map(&maps.v8, io.v, io.kv_rows, D, D, 8);
-    const bool tile128 = io.kv_rows >= kBN;
-    if (!rc) rc = make_map(&maps.k128, io.k, io.kv_rows, D, D, tile128 ? kBN : 8);
-    if (!rc) rc = make_map(&maps.v128, io.v, io.kv_rows, D, D, tile128 ? kBN : 8);
-    const bool arena_tma = io.arena && io.arena_rows >= 8;
-    if (!rc) rc = make_map(&maps.a8, arena_tma ? io.arena : io.k, arena_tma ? io.arena_rows : io.kv_rows,
-                           arena_tma ? 2 * D : D, arena_tma ? 2 * D : D, 8);
+    for (int i = 0; !rc && i < kBoxKinds; ++i) {
+        const uint32_t h = 8u << (i < base_boxes ? i : 0);
+        rc = make_map(&maps.kv[0][i], io.k, io.kv_rows, D, D, h);
+        if (!rc) rc = make_map(&maps.kv[1][i], io.v, io.kv_rows, D, D, h);
+        if (!rc && arena_boxes)
+            rc = make_map(&maps.a[i], io.arena, io.arena_rows, 2 * D, 2 * D, 8u << (i < arena_boxes ? i : 0));
+    }
     if (rc) return rc;
+    if (base_boxes == 0 || io.q_rows < 8) {
+        set_error("attn_bf16: Q and K/V need at least 8 rows");
+        return KVP_ERR_ARG;
+    }
 
     Params P;
     std::memset(&P, 0, sizeof P);
@@ -777,11 +845,20 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
     P.flat = d.flat;
     P.n_qt = (int)((T + kBM - 1) / kBM);
     P.items_per_head = d.flat ? (int)((d.frames * T + kBM - 1) / kBM) : d.frames * P.n_qt;
-    P.use_tile128 = tile128 ? 1 : 0;
-    P.arena_tma = arena_tma ? 1 : 0;
+    P.base_boxes = base_boxes;
+    P.arena_boxes = arena_boxes;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)kDH);
 
-    const int smem = (int)sizeof(Smem) + 1024;
+    const int smem = (int)sizeof(Smem);
+    {
+        int dev = 0, optin = 0;
+        KVP_CUDA(cudaGetDevice(&dev));
+        KVP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        if (smem > optin) {
+            set_error("attn_bf16: needs %d B of shared memory per block, device allows %d", smem, optin);
+            return KVP_ERR_UNSUPPORTED;
+        }
+    }
     static int configured_smem = 0;
     if (configured_smem != smem) {
         KVP_CUDA(cudaFuncSetAttribute(attn_bf16_sm100_kernel,

@@ -9,6 +9,7 @@ namespace kvp {
 // Bits of the device status word (kvp_read_status).
 constexpr int KVP_STATUS_MAP = 1;      // a KVMap entry pointed outside the arena (base row read)
 constexpr int KVP_STATUS_TIMEOUT = 2;  // a bounded wait expired; the CTA's output is incomplete
+constexpr int KVP_STATUS_ALIGN = 4;    // dynamic shared memory not 1024-byte aligned; nothing computed
 
 // One layer's buffers.  Q/K/V/Out are bf16 [rows][D] (head h at columns
 // [h*128, h*128+128)); the arena is bf16 [arena_rows][2*D] (K half, V half);

@@ -49,7 +49,7 @@ class StackRank:
     def __init__(self, *, p0: int, p1: int, heads: int = 12, frames: int = 21,
                  tokens: int = 1560, policy: str = "reuse_weighted", set_aside: int,
                  streaming: bool = False, device="cuda", seed: int = 0, tile_tokens: int = 16,
-                 make_data: bool = True):
+                 make_data: bool = True, window: bool = True):
         self.heads, self.frames, self.tokens = heads, frames, tokens
         self.policy = policy
         self.rows = frames * tokens
@@ -78,6 +78,9 @@ class StackRank:
                 self.chunks[ci].slot = slot
             self.sessions.append(s)
         self.persist = policy != "none"
+        # window=False keeps the arena and the KVMap but sets no persisting
+        # access-policy window (measures what persistence itself contributes)
+        self.use_window = window
 
     @property
     def n_pairs(self) -> int:
@@ -102,7 +105,8 @@ class StackRank:
     def attend(self, c: Chunk, stream: int) -> None:
         s = self.sessions[c.session]
         if self.persist:
-            s.window(c.slot, stream)
+            if self.use_window:
+                s.window(c.slot, stream)
             attn_bf16(c.q, c.k, c.v, c.o, tokens=self.tokens, frames=self.frames,
                       heads=c.nheads, mode="causal", flat=True, kvmap_ptr=s.device_map_ptr(),
                       arena_ptr=s.arena_ptr(c.slot), arena_rows=s.cap_rows, stream=stream)
@@ -114,5 +118,5 @@ class StackRank:
         self.plan_and_stage(scores, stream)
         for c in self.chunks:
             self.attend(c, stream)
-        if self.persist:
+        if self.persist and self.use_window:
             self.sessions[0].clear_window(stream)
