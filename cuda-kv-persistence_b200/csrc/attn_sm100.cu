@@ -10,23 +10,32 @@
 // never depends on where a row came from, so outputs are bitwise identical
 // across policies.
 //
-// CTA = 128 query rows x one head.  Warp roles (256 threads):
-//   warp 0      producer: reads the KVMap for each 128-key tile, classifies
-//               every 8-row group (all base / one ascending arena run /
-//               mixed) and stages K and V with TMA boxes (128 rows when the
-//               whole tile is base rows, 8 rows per group otherwise); mixed
-//               groups and padding are copied with 16-byte loads into the
-//               same 128B-swizzled layout
-//   warp 1      TMEM allocation and the single-thread MMA issuer:
-//               S_j = Q K_j^T (M128 N128 K16 x8) and O += P_{j-1} V_{j-1}
-//   warps 4-7   softmax (thread i owns query row i = TMEM lane i), online
-//               max with lazy rescaling (only when the max grows by > 8 in
-//               log2 units), P written to shared memory as bf16, then the
-//               epilogue O / l -> bf16 -> global
-// TMEM columns: S ring of three 128-column accumulators [0,384), O [384,512).  Shared memory: Q
-// 32 KB, two K|V stages of 64 KB, P 32 KB.  Every mbarrier wait is bounded
-// (about one second of %globaltimer); on expiry the CTA records
-// KVP_STATUS_TIMEOUT in the status word and unwinds without hanging.
+// CTA = two 128-row query tiles (Q0, Q1) x one head; both tiles consume the
+// same stream of 128-key K/V tiles, so every staged K/V tile feeds four
+// 128x128x128 GEMMs.  Warp roles (384 threads):
+//   warp 0      Q loads and the K producer, warp 2 the V producer: each reads
+//               the KVMap for its 128-key tile, classifies every 8-row group
+//               (all base / one ascending arena run / mixed) and stages the
+//               tile with TMA boxes (one 128-row box per panel when the whole
+//               tile is base rows, power-of-two boxes per run otherwise);
+//               mixed groups and padding are copied with 16-byte loads into
+//               the same 128B-swizzled layout
+//   warp 1      TMEM allocation and the single-thread MMA issuer, in the
+//               order S0_j, PV1_{j-1}, S1_j, PV0_j: while one tile's softmax
+//               runs, the tensor cores work on the other tile
+//   warps 4-7   softmax of Q0, warps 8-11 softmax of Q1: thread i owns query
+//               row i (TMEM lane i) and all 128 columns of each S tile.
+//               Exponentials are computed with the running max first; only a
+//               row whose tile sum exceeds 256 (its max grew by more than 8 in
+//               log2 units) recomputes with the new max and rescales O.  P is
+//               written back into the first 64 columns of its own S
+//               accumulator as packed bf16 and read from there by the PV MMA.
+//               The same warps run the epilogue O / l -> bf16 -> global.
+// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512).
+// Shared memory: Q0, Q1 (32 KB each), a K ring of two and a V ring of three
+// 32 KB stages.  Every mbarrier wait is bounded (about one second of
+// %globaltimer); on expiry the CTA records KVP_STATUS_TIMEOUT in the status
+// word and unwinds without hanging.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -41,32 +50,36 @@ namespace kvp {
 
 namespace {
 
-constexpr int kBM = 128;           // query rows per CTA
+constexpr int kBM = 128;           // query rows per query tile
+constexpr int kQTiles = 2;         // query tiles per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kDH = 128;           // head dim
-constexpr int kStages = 2;         // depth of the K ring and of the V ring
-constexpr int kSBuf = 3;           // S accumulators in TMEM: S runs two tiles ahead of PV
-constexpr int kThreads = 384;     // producer, MMA, 2 idle, 8 softmax warps
+constexpr int kKStages = 2;        // depth of the K ring
+constexpr int kVStages = 3;        // depth of the V ring (V_j stays until PV1_j, one tile later)
+constexpr int kThreads = 384;      // producers, MMA, 1 idle, 2 x 4 softmax warps
 constexpr uint32_t kPanel = 128 * 128;        // one [128 rows][64 bf16] swizzled panel
 constexpr uint32_t kTileBytes = 2 * kPanel;   // [128][128] bf16
 constexpr uint32_t kGroupPanel = 8 * 128;     // one 8-row group of a panel
 constexpr unsigned long long kWaitNs = 1000000000ull;  // bounded waits: ~1 s
+constexpr uint32_t kSuspendNs = 200000;                 // longest single hardware suspend in a wait
+constexpr int kRegsLow = 104;      // registers per thread, warps 0-3 (producers, MMA)
+constexpr int kRegsHigh = 200;     // registers per thread, warps 4-11 (softmax)
+static_assert(kRegsLow * 128 + 2 * kRegsHigh * 128 <= 65536, "register split exceeds the SM");
+constexpr float kRedoSum = 256.f;  // a tile row sum above this recomputes with the new max
 
 struct __align__(1024) Smem {
-    uint8_t q[kTileBytes];
-    uint8_t k[kStages][kTileBytes];
-    uint8_t v[kStages][kTileBytes];
-    uint8_t p[2][kTileBytes];       // P double buffer: tile j uses p[j & 1]
-    uint64_t bar_q;
-    uint64_t bar_full[2][kStages];   // [0] = K ring, [1] = V ring
-    uint64_t bar_empty[2][kStages];
-    uint64_t bar_s_full[kSBuf];
-    uint64_t bar_s_free[kSBuf];
-    uint64_t bar_p_full[2];         // P_j written into p[j & 1]
-    uint64_t bar_pv_done[2];        // PV_j done -> p[j & 1] free (one barrier per buffer)
-    uint64_t bar_red[4][2];      // row-max exchange of the two warps of a row block
-    uint64_t bar_sum[4];         // final row-sum exchange
-    float red[2][2][128];        // [tile parity][half][row] partial row max
+    uint8_t q[kQTiles][kTileBytes];
+    uint8_t k[kKStages][kTileBytes];
+    uint8_t v[kVStages][kTileBytes];
+    uint64_t bar_q[kQTiles];
+    uint64_t bar_kfull[kKStages];
+    uint64_t bar_kempty[kKStages];
+    uint64_t bar_vfull[kVStages];
+    uint64_t bar_vempty[kVStages];
+    uint64_t bar_s_full[kQTiles];   // S_q(j) landed (and, by issue order, PV_q(j-1) too)
+    uint64_t bar_p_full[kQTiles];   // P_q(j) in TMEM, S_q(j) read, O_q rescaled
+    uint64_t bar_o_done[kQTiles];   // last PV_q landed
+    uint64_t bar_mma_done;          // every issued MMA landed (TMEM may be freed)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -87,7 +100,7 @@ struct Params {
     __nv_bfloat16* out;
     int* status;
     long long q_rows, kv_rows, arena_rows;
-    int D, T, frames, q_frame0, mode, window, head0, nheads, flat, items_per_head, n_qt;
+    int D, T, frames, q_frame0, mode, window, head0, nheads, flat, items_per_head, n_qt, n_pairs;
     int base_boxes, arena_boxes;   // box kinds usable (heights <= tensor rows); 0 = no arena TMA
     float scale_log2;
 };
@@ -124,33 +137,51 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
         : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
     return ok != 0;
 }
+// try_wait that lets the hardware suspend the thread until the phase
+// completes (or kSuspendNs passes), so a waiting warp takes no issue slots
+// from the softmax warps that share its SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(b)), "r"(parity), "r"(kSuspendNs) : "memory");
+    return ok != 0;
+}
 // Bounded wait.  Returns false (and raises the CTA abort flag and the global
 // status) when the phase did not complete within kWaitNs, or when another
 // role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, Smem& sm, int* status) {
     if (mbar_try_wait(b, parity)) return true;
     const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(b, parity)) return true;
-        if ((it & 63u) == 0) {
-            if (*(volatile int*)&sm.abort_flag) return false;
-            if (globaltimer() - t0 > kWaitNs) {
-                *(volatile int*)&sm.abort_flag = 1;
-                atomicOr(status, KVP_STATUS_TIMEOUT);
-                return false;
-            }
+    for (;;) {
+        if (mbar_try_wait_sleep(b, parity)) return true;
+        if (*(volatile int*)&sm.abort_flag) return false;
+        if (globaltimer() - t0 > kWaitNs) {
+            *(volatile int*)&sm.abort_flag = 1;
+            atomicOr(status, KVP_STATUS_TIMEOUT);
+            return false;
         }
     }
 }
-// Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast, so the
-// warp stays converged for the .sync.aligned tcgen05 and shuffle
-// instructions that follow.
+// Warp-uniform bounded wait: every lane polls and the verdicts are combined
+// (a completed phase stays completed until this warp itself moves the
+// protocol on), so the warp stays converged for the .sync.aligned tcgen05
+// and shuffle instructions that follow.
 __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t parity, Smem& sm, int* status) {
-    bool ok = true;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(b, parity, sm, status);
-    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    __syncwarp();
-    return ok;
+    if (__any_sync(0xffffffffu, mbar_try_wait(b, parity))) return true;
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+        if (__any_sync(0xffffffffu, mbar_try_wait_sleep(b, parity))) return true;
+        if (__any_sync(0xffffffffu, *(volatile int*)&sm.abort_flag != 0)) return false;
+        if (__any_sync(0xffffffffu, globaltimer() - t0 > kWaitNs)) {
+            if ((threadIdx.x & 31) == 0) {
+                *(volatile int*)&sm.abort_flag = 1;
+                atomicOr(status, KVP_STATUS_TIMEOUT);
+            }
+            __syncwarp();
+            return false;
+        }
+    }
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -178,6 +209,16 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, 
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// O_tmem (+)= A_tmem * B_smem: A read from tensor memory (K-major, two bf16
+// per 32-bit column, row i in lane i), B described in shared memory.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
 #define KVP_TMEM_LD32(taddr, r)                                                                  \
@@ -237,9 +278,12 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // relative error (max relative error 1.4e-4 over x in [-126, 8], against bf16's
 // 3.9e-3 rounding of P), 2^n added to the exponent bits.  Inputs below -126
 // are clamped to -126 (the result stays a positive number below 2^-125,
-// which is 0 in the bf16 P and negligible in the row sum; -inf lands there too).
+// negligible in the row sum and against any unmasked P; -inf lands there
+// too), inputs above 127 to 127 (a finite 2^127-ish value, so an overgrown
+// speculative exponent still shows up in the row sum instead of wrapping
+// the exponent bits).
 __device__ __forceinline__ float ex2_poly(float x) {
-    x = fmaxf(x, -126.f);
+    x = fminf(fmaxf(x, -126.f), 127.f);
     const float t = x + 12582912.f;           // 1.5 * 2^23: round to nearest integer
     const float f = x - (t - 12582912.f);
     float p = fmaf(5.517162719e-02f, f, 2.426111432e-01f);
@@ -254,14 +298,64 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot per pair).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// ex2_poly on a pair, the arithmetic in f32x2 (same fit, same clamps).
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+    const uint64_t x = f2_pack(fminf(fmaxf(x0, -126.f), 127.f), fminf(fmaxf(x1, -126.f), 127.f));
+    const uint64_t magic = f2_pack(12582912.f, 12582912.f);
+    const uint64_t t = f2_add(x, magic);
+    const uint64_t f = f2_sub(x, f2_sub(t, magic));
+    uint64_t q = f2_fma(f2_pack(5.517162719e-02f, 5.517162719e-02f), f, f2_pack(2.426111432e-01f, 2.426111432e-01f));
+    q = f2_fma(q, f, f2_pack(6.932609953e-01f, 6.932609953e-01f));
+    q = f2_fma(q, f, f2_pack(9.999280725e-01f, 9.999280725e-01f));
+    float t0, t1, q0, q1;
+    f2_unpack(t, t0, t1);
+    f2_unpack(q, q0, q1);
+    // t = 1.5*2^23 + n has bits 0x4B400000 + n, and 0x4B400000 << 23 wraps to
+    // zero, so (bits(t) << 23) == n << 23.
+    y0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+    y1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
 // --------------------------------------------------------------- work item
+struct QTile {
+    long long row0;      // first query row (absolute in Q/out)
+    int nq;              // valid query rows (<= 128); 0 = empty tile
+    int n_tiles;         // 128-key tiles this query tile consumes
+    long long khi;       // key rows [klo, khi) for rows >= split
+    long long khi_lo;    // key limit of rows < split (flat tiles crossing a frame)
+    int split;
+};
+
 struct Work {
-    long long q_row0;    // first query row (absolute in Q/out)
-    int nq;              // valid query rows (<= 128)
-    long long klo, khi;  // key rows [klo, khi) for rows >= split
-    int split;           // rows < split use khi_lo (flat tiles crossing a frame)
-    long long khi_lo;
     int head;
+    long long klo;       // first key row, shared by both query tiles
+    long long khi;       // end of the staged key rows (max over the tiles)
+    int n_tiles;         // K/V tiles staged (max over the tiles)
+    QTile t[kQTiles];
 };
 
 __device__ __forceinline__ Work decode_work(const Params& P) {
@@ -274,31 +368,122 @@ __device__ __forceinline__ Work decode_work(const Params& P) {
         const long long R0 = (long long)P.q_frame0 * T;
         const long long R1 = (long long)(P.q_frame0 + P.frames) * T;
         const long long t = (long long)(P.items_per_head - 1 - i);  // longest first
-        w.q_row0 = R0 + t * kBM;
-        const long long last = (w.q_row0 + kBM < R1 ? w.q_row0 + kBM : R1) - 1;
-        w.nq = (int)(last - w.q_row0 + 1);
-        const long long fl = last / T, ff = w.q_row0 / T;
         w.klo = 0;
-        w.khi = (fl + 1) * T;
-        w.split = ff != fl ? (int)(fl * T - w.q_row0) : 0;
-        w.khi_lo = (ff + 1) * T;
+#pragma unroll
+        for (int q = 0; q < kQTiles; ++q) {
+            QTile& x = w.t[q];
+            x.row0 = R0 + (t * kQTiles + q) * kBM;
+            if (x.row0 >= R1) {
+                x.nq = 0; x.n_tiles = 0; x.khi = x.khi_lo = 0; x.split = 0;
+                continue;
+            }
+            const long long last = (x.row0 + kBM < R1 ? x.row0 + kBM : R1) - 1;
+            x.nq = (int)(last - x.row0 + 1);
+            const long long fl = last / T, ff = x.row0 / T;
+            x.khi = (fl + 1) * T;
+            x.split = ff != fl ? (int)(fl * T - x.row0) : 0;
+            x.khi_lo = (ff + 1) * T;
+        }
     } else {
-        const int fr = i / P.n_qt, qt = i % P.n_qt;
+        const int fr = i / P.n_pairs, pr = i % P.n_pairs;
         const int f = P.q_frame0 + P.frames - 1 - fr;  // longest key span first
-        w.q_row0 = (long long)f * T + (long long)qt * kBM;
-        const long long left = T - (long long)qt * kBM;
-        w.nq = (int)(left < kBM ? left : kBM);
         if (P.mode == 0) {
             w.klo = (long long)f * T;
         } else {
             const int base = P.window > 0 ? (f - P.window + 1 > 0 ? f - P.window + 1 : 0) : 0;
             w.klo = (long long)base * T;
         }
-        w.khi = (long long)(f + 1) * T;
-        w.split = 0;
-        w.khi_lo = w.khi;
+#pragma unroll
+        for (int q = 0; q < kQTiles; ++q) {
+            QTile& x = w.t[q];
+            const int qt = pr * kQTiles + q;
+            x.row0 = (long long)f * T + (long long)qt * kBM;
+            const long long left = T - (long long)qt * kBM;
+            x.nq = qt < P.n_qt ? (int)(left < kBM ? left : kBM) : 0;
+            x.khi = x.khi_lo = (long long)(f + 1) * T;
+            x.split = 0;
+        }
+    }
+    w.khi = w.klo;
+    w.n_tiles = 0;
+#pragma unroll
+    for (int q = 0; q < kQTiles; ++q) {
+        QTile& x = w.t[q];
+        if (x.nq > 0) {
+            x.n_tiles = (int)((x.khi - w.klo + kBN - 1) / kBN);
+            if (x.khi > w.khi) w.khi = x.khi;
+        } else {
+            x.n_tiles = 0;
+        }
+        if (x.n_tiles > w.n_tiles) w.n_tiles = x.n_tiles;
     }
     return w;
+}
+
+// ----------------------------------------------------------- softmax pieces
+// One S row (this thread's TMEM lane, 128 columns) -> P = 2^(s*sl2 - m) as
+// packed bf16 pairs in pk, returns the fp32 row sum of P.  Columns at or
+// past `left` are masked (-inf) when kMask.  A quarter of the exponentials
+// run on the FMA pipe (ex2_poly2), the rest on MUFU; scaling and the row sum
+// use f32x2 arithmetic.
+template <bool kMask>
+__device__ __forceinline__ float exp_row(uint32_t s_addr, float m, float sl2, int left, uint32_t (&pk)[64]) {
+    const uint64_t sl2x2 = f2_pack(sl2, sl2);
+    const uint64_t negm2 = f2_pack(-m, -m);
+    uint64_t acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = 0ull;   // (+0, +0)
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+        uint32_t sr[32];
+        KVP_TMEM_LD32(s_addr + 32 * h, sr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+            float s0 = __uint_as_float(sr[c]);
+            float s1 = __uint_as_float(sr[c + 1]);
+            if (kMask) {
+                if (32 * h + c >= left) s0 = -INFINITY;
+                if (32 * h + c + 1 >= left) s1 = -INFINITY;
+            }
+            float x0, x1, p0, p1;
+            f2_unpack(f2_fma(f2_pack(s0, s1), sl2x2, negm2), x0, x1);
+            if ((c & 7) == 6) {
+                ex2_poly2(x0, x1, p0, p1);
+            } else {
+                p0 = ex2_approx(x0);
+                p1 = ex2_approx(x1);
+            }
+            acc[(c >> 1) & 3] = f2_add(acc[(c >> 1) & 3], f2_pack(p0, p1));
+            pk[16 * h + (c >> 1)] = pack_bf16(p0, p1);
+        }
+    }
+    const uint64_t a2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+    float lo, hi;
+    f2_unpack(a2, lo, hi);
+    return lo + hi;
+}
+
+// Row max of one S row (raw scores), masked as in exp_row.
+template <bool kMask>
+__device__ __forceinline__ float max_row(uint32_t s_addr, int left) {
+    float mx[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+        uint32_t sr[32];
+        KVP_TMEM_LD32(s_addr + 32 * h, sr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            float s = __uint_as_float(sr[c]);
+            if (kMask && 32 * h + c >= left) s = -INFINITY;
+            mx[c & 7] = fmaxf(mx[c & 7], s);
+        }
+    }
+    return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
 }
 
 // ------------------------------------------------------------------ kernel
@@ -306,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_constant__ Params P) {
     extern __shared__ uint8_t smem_raw[];
     // The layout needs a 1024-byte aligned base (128B-swizzle atoms) and uses
-    // the whole 227 KB, so there is no room to realign: refuse instead.
+    // nearly all of the 227 KB, so there is no room to realign: refuse instead.
     if (reinterpret_cast<uintptr_t>(smem_raw) & 1023) {
         if (threadIdx.x == 0) atomicOr(P.status, KVP_STATUS_ALIGN);
         return;
@@ -315,28 +500,24 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const Work w = decode_work(P);
-    const int n_tiles = (int)((w.khi - w.klo + kBN - 1) / kBN);
+    const int n_tiles = w.n_tiles;
 
     if (threadIdx.x == 0) {
-        mbar_init(&sm.bar_q, 1);
-        for (int op = 0; op < 2; ++op)
-            for (int s = 0; s < kStages; ++s) {
-                mbar_init(&sm.bar_full[op][s], 1);
-                mbar_init(&sm.bar_empty[op][s], 1);
-            }
-        for (int b = 0; b < kSBuf; ++b) {
-            mbar_init(&sm.bar_s_full[b], 1);
-            mbar_init(&sm.bar_s_free[b], 256);
+        for (int q = 0; q < kQTiles; ++q) {
+            mbar_init(&sm.bar_q[q], 1);
+            mbar_init(&sm.bar_s_full[q], 1);
+            mbar_init(&sm.bar_p_full[q], 128);
+            mbar_init(&sm.bar_o_done[q], 1);
         }
-        mbar_init(&sm.bar_p_full[0], 256);
-        mbar_init(&sm.bar_p_full[1], 256);
-        mbar_init(&sm.bar_pv_done[0], 1);
-        mbar_init(&sm.bar_pv_done[1], 1);
-        for (int g = 0; g < 4; ++g) {
-            mbar_init(&sm.bar_red[g][0], 64);
-            mbar_init(&sm.bar_red[g][1], 64);
-            mbar_init(&sm.bar_sum[g], 64);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&sm.bar_kfull[s], 1);
+            mbar_init(&sm.bar_kempty[s], 1);
         }
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(&sm.bar_vfull[s], 1);
+            mbar_init(&sm.bar_vempty[s], 1);
+        }
+        mbar_init(&sm.bar_mma_done, 1);
         sm.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async_smem();
@@ -352,29 +533,44 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
     const uint32_t tmem = sm.tmem_base;
     const int D = P.D;
     const int hcol = w.head * kDH;
-
+    // Register split: the producer / MMA warpgroup hands registers to the two
+    // softmax warpgroups.  The host checks before launch that the kernel's
+    // register pool covers kRegsLow * 128 + 2 * kRegsHigh * 128, so the
+    // increase never waits on registers that do not exist.
+    // (Each role branch sets its own limit, so no code is compiled for both.)
+    if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
     if (warp == 0 || warp == 2) {
         // ============================ producers ===============================
         // Warp 0 stages Q and the K ring, warp 2 the V ring; each reads the
         // KVMap rows of its tile itself, so K of tile j+2 can load as soon as
-        // S_j = Q K_j^T is done, independently of the slower V ring.
+        // S1_j = Q1 K_j^T is done, independently of the V ring.
         const int op = warp == 0 ? 0 : 1;
         if (op == 0 && lane == 0) {
             // Q: 8-row groups that start inside the tensor come by TMA (a group
             // running past the end is zero-filled by TMA); groups wholly past
             // q_rows are not loaded -- their rows only feed output rows that are
             // never stored (S, P and O are row-independent).
-            uint32_t qbytes = 0;
-            for (int g = 0; g < kBM / 8; ++g)
-                if (w.q_row0 + 8 * g < P.q_rows) qbytes += 2 * kGroupPanel;
-            mbar_arrive_expect_tx(&sm.bar_q, qbytes);
-            for (int g = 0; g < kBM / 8; ++g) {
-                if (w.q_row0 + 8 * g >= P.q_rows) break;
-                for (int p = 0; p < 2; ++p)
-                    tma_load_2d(sm.q + p * kPanel + g * kGroupPanel, &maps.q8, hcol + 64 * p,
-                                (int)(w.q_row0 + 8 * g), &sm.bar_q);
+#pragma unroll
+            for (int q = 0; q < kQTiles; ++q) {
+                if (w.t[q].n_tiles == 0) continue;
+                const long long qr0 = w.t[q].row0;
+                uint32_t qbytes = 0;
+                for (int g = 0; g < kBM / 8; ++g)
+                    if (qr0 + 8 * g < P.q_rows) qbytes += 2 * kGroupPanel;
+                mbar_arrive_expect_tx(&sm.bar_q[q], qbytes);
+                for (int g = 0; g < kBM / 8; ++g) {
+                    if (qr0 + 8 * g >= P.q_rows) break;
+                    for (int p = 0; p < 2; ++p)
+                        tma_load_2d(sm.q[q] + p * kPanel + g * kGroupPanel, &maps.q8, hcol + 64 * p,
+                                    (int)(qr0 + 8 * g), &sm.bar_q[q]);
+                }
             }
         }
+        const int n_st = op == 0 ? kKStages : kVStages;
+        uint64_t* bar_full = op == 0 ? sm.bar_kfull : sm.bar_vfull;
+        uint64_t* bar_empty = op == 0 ? sm.bar_kempty : sm.bar_vempty;
+        uint8_t* ring = op == 0 ? sm.k[0] : sm.v[0];
         const CUtensorMap* base_maps = maps.kv[op];
         const __nv_bfloat16* base = op == 0 ? P.k : P.v;
         const int acol = (op == 0 ? 0 : D) + hcol;     // column of this operand in an arena row
@@ -394,9 +590,9 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         for (int j = 0; j < n_tiles; ++j) {
             long long m[4] = {m_next[0], m_next[1], m_next[2], m_next[3]};
             map_rows(j + 1, m_next);
-            const int s = j % kStages;
-            const uint32_t ph = (uint32_t)(j / kStages) & 1u;
-            if (!warp_wait(&sm.bar_empty[op][s], ph ^ 1u, sm, P.status)) break;
+            const int s = j % n_st;
+            const uint32_t ph = (uint32_t)(j / n_st) & 1u;
+            if (!warp_wait(&bar_empty[s], ph ^ 1u, sm, P.status)) break;
             const long long r0 = w.klo + (long long)j * kBN;
             // Lane l classifies rows 4l..4l+3; lanes 2g, 2g+1 form 8-row group g.
             bool pad[4];
@@ -435,8 +631,8 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 ((g_base && ((base_mask >> (lane - 2)) & 1u)) ||
                  (g_arena && ((arena_mask >> (lane - 2)) & 1u) && m[0] == prev_m0 + 8));
             const unsigned cont_mask = __ballot_sync(0xffffffffu, cont);
-            uint8_t* dst_tile = op == 0 ? sm.k[s] : sm.v[s];
-            uint64_t* full = &sm.bar_full[op][s];
+            uint8_t* dst_tile = ring + (size_t)s * kTileBytes;
+            uint64_t* full = &bar_full[s];
             if (lane == 0) {
                 uint32_t bytes = 0;
                 if (whole_base) {
@@ -511,207 +707,154 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         }
         // Drain: never leave TMA writes in flight into a CTA that is exiting.
         if (lane == 0 && sm.abort_flag) {
-            for (int j = last_armed > 0 ? last_armed - 1 : 0; j <= last_armed; ++j) {
+            for (int j = last_armed - n_st + 1; j <= last_armed; ++j) {
                 if (j < 0) continue;
                 const unsigned long long t0 = globaltimer();
-                while (!mbar_try_wait(&sm.bar_full[op][j % kStages], (uint32_t)(j / kStages) & 1u) &&
+                while (!mbar_try_wait(&bar_full[j % n_st], (uint32_t)(j / n_st) & 1u) &&
                        globaltimer() - t0 < kWaitNs) {
                 }
             }
+            if (op == 0)
+                for (int q = 0; q < kQTiles; ++q) {
+                    if (w.t[q].n_tiles == 0) continue;
+                    const unsigned long long t0 = globaltimer();
+                    while (!mbar_try_wait(&sm.bar_q[q], 0) && globaltimer() - t0 < kWaitNs) {
+                    }
+                }
         }
     } else if (warp == 1) {
         // ============================ MMA issuer ==============================
+        // Per K/V tile j: S0_j, PV1_{j-1}, S1_j, PV0_j.  tcgen05.mma from one
+        // thread executes in issue order, so S_q(j+1) (which overwrites the P
+        // columns of S_q) runs after PV_q(j) has read them, and the commit of
+        // S_q(j) also covers PV_q(j-1): the softmax may rescale O_q as soon as
+        // S_q(j) is visible.
         if (lane == 0) {
-            const uint32_t q_s = smem_u32(sm.q);
-            const uint32_t p_s0 = smem_u32(sm.p[0]);
             constexpr uint32_t idS = idesc_bf16(false);
             constexpr uint32_t idO = idesc_bf16(true);
-            const uint32_t tmem_o = tmem + 128 * kSBuf;
-            bool ok = mbar_wait(&sm.bar_q, 0, sm, P.status);
-            int issued_pv = 0;
-            for (int j = 0; ok && j <= n_tiles + kSBuf - 2; ++j) {
-                if (j < n_tiles) {
-                    const int s = j % kStages, b = j % kSBuf;
-                    if (!mbar_wait(&sm.bar_full[0][s], (uint32_t)(j / kStages) & 1u, sm, P.status)) { ok = false; break; }
-                    if (!mbar_wait(&sm.bar_s_free[b], ((uint32_t)(j / kSBuf) & 1u) ^ 1u, sm, P.status)) { ok = false; break; }
+            const int n0 = w.t[0].n_tiles, n1 = w.t[1].n_tiles;
+            bool ok = true;
+            bool q_ready[kQTiles] = {false, false};
+            auto s_mma = [&](int q, int sK) -> bool {
+                if (!q_ready[q]) {
+                    if (!mbar_wait(&sm.bar_q[q], 0, sm, P.status)) return false;
+                    q_ready[q] = true;
                     tc_fence_after();
-                    const uint32_t k_s = smem_u32(sm.k[s]);
-#pragma unroll
-                    for (int ks = 0; ks < kDH / 16; ++ks) {
-                        const uint32_t off = (uint32_t)(ks >> 2) * kPanel + (uint32_t)(ks & 3) * 32;
-                        tc_mma(tmem + 128 * b, sw128_desc(q_s + off, 16, 1024),
-                               sw128_desc(k_s + off, 16, 1024), idS, ks > 0 ? 1u : 0u);
-                    }
-                    tc_commit(&sm.bar_s_full[b]);
-                    tc_commit(&sm.bar_empty[0][s]);   // K_j consumed: the K ring moves on
                 }
-                if (j >= kSBuf - 1 && j - (kSBuf - 1) < n_tiles) {
-                    const int jp = j - (kSBuf - 1), s = jp % kStages;
-                    if (!mbar_wait(&sm.bar_full[1][s], (uint32_t)(jp / kStages) & 1u, sm, P.status)) { ok = false; break; }
-                    if (!mbar_wait(&sm.bar_p_full[jp & 1], (uint32_t)(jp >> 1) & 1u, sm, P.status)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t v_s = smem_u32(sm.v[s]);
+                const uint32_t q_s = smem_u32(sm.q[q]);
+                const uint32_t k_s = smem_u32(sm.k[sK]);
 #pragma unroll
-                    for (int ks = 0; ks < kBN / 16; ++ks) {
-                        const uint32_t a_off = (uint32_t)(ks >> 2) * kPanel + (uint32_t)(ks & 3) * 32;
-                        tc_mma(tmem_o, sw128_desc(p_s0 + (uint32_t)(jp & 1) * kTileBytes + a_off, 16, 1024),
-                               sw128_desc(v_s + (uint32_t)ks * 2048, kPanel, 1024), idO,
-                               (jp > 0 || ks > 0) ? 1u : 0u);
-                    }
-                    tc_commit(&sm.bar_empty[1][s]);
-                    tc_commit(&sm.bar_pv_done[jp & 1]);
-                    issued_pv = jp + 1;
+                for (int ks = 0; ks < kDH / 16; ++ks) {
+                    const uint32_t off = (uint32_t)(ks >> 2) * kPanel + (uint32_t)(ks & 3) * 32;
+                    tc_mma(tmem + 128u * q, sw128_desc(q_s + off, 16, 1024),
+                           sw128_desc(k_s + off, 16, 1024), idS, ks > 0 ? 1u : 0u);
                 }
+                tc_commit(&sm.bar_s_full[q]);
+                return true;
+            };
+            auto pv_mma = [&](int q, int jv) -> bool {
+                const int sV = jv % kVStages;
+                if (!mbar_wait(&sm.bar_vfull[sV], (uint32_t)(jv / kVStages) & 1u, sm, P.status)) return false;
+                if (!mbar_wait(&sm.bar_p_full[q], (uint32_t)jv & 1u, sm, P.status)) return false;
+                tc_fence_after();
+                const uint32_t v_s = smem_u32(sm.v[sV]);
+#pragma unroll
+                for (int ks = 0; ks < kBN / 16; ++ks)
+                    tc_mma_ts(tmem + 256u + 128u * q, tmem + 128u * q + 8u * ks,
+                              sw128_desc(v_s + (uint32_t)ks * 2048, kPanel, 1024), idO,
+                              (jv > 0 || ks > 0) ? 1u : 0u);
+                if (jv == (q ? n1 : n0) - 1) tc_commit(&sm.bar_o_done[q]);
+                if (q == 1 || jv >= n1) tc_commit(&sm.bar_vempty[sV]);   // last reader of V_jv
+                return true;
+            };
+            for (int j = 0; ok && j < n_tiles; ++j) {
+                const int sK = j % kKStages;
+                if (!mbar_wait(&sm.bar_kfull[sK], (uint32_t)(j / kKStages) & 1u, sm, P.status)) { ok = false; break; }
+                tc_fence_after();
+                if (j < n0 && !s_mma(0, sK)) { ok = false; break; }
+                if (j >= 1 && j - 1 < n1 && !pv_mma(1, j - 1)) { ok = false; break; }
+                if (j < n1 && !s_mma(1, sK)) { ok = false; break; }
+                tc_commit(&sm.bar_kempty[sK]);
+                if (j < n0 && !pv_mma(0, j)) { ok = false; break; }
             }
-            // Drain: the last committed PV must land before TMEM is freed.
-            if (issued_pv > 0) {
-                const unsigned long long t0 = globaltimer();
-                const int last = issued_pv - 1;
-                while (!mbar_try_wait(&sm.bar_pv_done[last & 1], (uint32_t)(last >> 1) & 1u) &&
-                       globaltimer() - t0 < kWaitNs) {
-                }
+            if (ok && n_tiles > 0 && n_tiles - 1 < n1) pv_mma(1, n_tiles - 1);
+            // Drain: every issued MMA lands before TMEM is freed.
+            tc_commit(&sm.bar_mma_done);
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try_wait(&sm.bar_mma_done, 0) && globaltimer() - t0 < kWaitNs) {
             }
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
         // ========================== softmax + epilogue ========================
-        // Warps 4-11: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
-        // quarter) and key columns [64*half, 64*half+64), half = (w-4)/4, of
-        // every S tile; the two warps of a row block exchange their partial
-        // row max through shared memory once per tile (named barrier of 64).
-        const int half = (warp - 4) >> 2;
-        const int row = (warp & 3) * 32 + lane;       // query row in tile == TMEM lane
+        const int qt = (warp - 4) >> 2;                // query tile of this warpgroup
+        const QTile t = qt ? w.t[1] : w.t[0];
+        const int row = (warp & 3) * 32 + lane;        // query row in tile == TMEM lane
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t col0 = 64u * (uint32_t)half;
-        const int rg = warp & 3;                       // row block shared with warp w^4
-        const long long my_khi = row < w.split ? w.khi_lo : w.khi;
+        const uint32_t s_tm = tmem + lane_base + 128u * qt;
+        const uint32_t o_tm = tmem + lane_base + 256u + 128u * qt;
+        const long long my_khi = row < t.split ? t.khi_lo : t.khi;
         const float sl2 = P.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;          // m in log2 units, scaled
         bool ok = true;
-        for (int j = 0; j < n_tiles; ++j) {
-            const int b = j & 1;           // parity buffer of the row-max exchange
-            const int sb = j % kSBuf;      // S accumulator of this tile
-            if (!warp_wait(&sm.bar_s_full[sb], (uint32_t)(j / kSBuf) & 1u, sm, P.status)) { ok = false; break; }
+        for (int j = 0; j < t.n_tiles; ++j) {
+            if (!warp_wait(&sm.bar_s_full[qt], (uint32_t)j & 1u, sm, P.status)) { ok = false; break; }
             tc_fence_after();
-            uint32_t sr[64];
-            const uint32_t s_addr = tmem + lane_base + 128 * sb + col0;
-            KVP_TMEM_LD32(s_addr + 0, (sr + 0));
-            KVP_TMEM_LD32(s_addr + 32, (sr + 32));
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&sm.bar_s_free[sb]);
-
-            float s[64];
-#pragma unroll
-            for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sr[c]);
-            const long long key0 = w.klo + (long long)j * kBN + col0;
-            const long long left = my_khi - key0;
-            if (left < 64) {   // tail tile: keys past the row's span never count
-#pragma unroll
-                for (int c = 0; c < 64; ++c)
-                    if (c >= left) s[c] = -INFINITY;
+            const long long left_ll = my_khi - (w.klo + (long long)j * kBN);
+            const int left = left_ll >= kBN ? kBN : (left_ll < 0 ? 0 : (int)left_ll);
+            const bool masked = !__all_sync(0xffffffffu, left == kBN);
+            uint32_t pk[64];
+            float rsum = 0.f;
+            float m_new = m_run;
+            // Exponentials against the running max; a row whose sum overgrows
+            // (its max rose by more than 8 in log2 units) triggers one redo of
+            // the warp with the new max.  The first tile takes the max first.
+            // One copy of each pass in the code.
+#pragma unroll 1
+            for (int attempt = 0;; ++attempt) {
+                if (attempt > 0 || j > 0)
+                    rsum = masked ? exp_row<true>(s_tm, m_new, sl2, left, pk)
+                                  : exp_row<false>(s_tm, m_new, sl2, left, pk);
+                const bool redo = attempt == 0 && (j == 0 || !(rsum <= kRedoSum));
+                if (!__any_sync(0xffffffffu, redo)) break;   // warp-uniform: tcgen05.ld is .sync.aligned
+                const float tmax = masked ? max_row<true>(s_tm, left) : max_row<false>(s_tm, left);
+                if (redo) m_new = fmaxf(m_run, tmax * sl2);
             }
-            // row max over this half: 8 independent chains, then a short tree
-            float mx8[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) mx8[i] = s[i];
-#pragma unroll
-            for (int c = 8; c < 64; c += 8)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(mx8[i], s[c + i]);
-            const float half_max = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                         fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            sm.red[b][half][row] = half_max;
-            mbar_arrive(&sm.bar_red[rg][b]);
-            // Lazy rescaling: keep the running max unless the row max grows by
-            // more than 8 (log2 units), so p <= 256 and O rarely needs a TMEM
-            // round trip.  After the first tile the exponentials are computed
-            // with the running max while the partner half's max is still in
-            // flight; only a row whose max jumps recomputes them.
-            float ps[8];
-            uint32_t pk[32];
-            auto exp_half = [&](float m) {
-                const float neg_m = -m;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-#pragma unroll
-                for (int c = 0; c < 64; c += 2) {
-                    const float x0 = fmaf(s[c], sl2, neg_m);
-                    const float x1 = fmaf(s[c + 1], sl2, neg_m);
-                    // a quarter of the exponentials run on the FMA pipe
-                    const bool fma_pipe = (c & 7) == 6;
-                    const float p0 = fma_pipe ? ex2_poly(x0) : ex2_approx(x0);
-                    const float p1 = fma_pipe ? ex2_poly(x1) : ex2_approx(x1);
-                    ps[(c >> 1) & 7] += p0 + p1;
-                    pk[c >> 1] = pack_bf16(p0, p1);
-                }
-            };
-            if (j > 0) exp_half(m_run);
-            if (!warp_wait(&sm.bar_red[rg][b], (uint32_t)(j >> 1) & 1u, sm, P.status)) { ok = false; break; }
-            const float tmax = fmaxf(half_max, sm.red[b][half ^ 1][row]) * sl2;  // both halves agree
-            float m_use = m_run, alpha = 1.f;
-            if (j == 0) {
-                m_use = tmax;
-                exp_half(m_use);
-            } else if (tmax > m_run + 8.f) {
-                m_use = tmax;
-                alpha = ex2_approx(m_run - tmax);
-                exp_half(m_use);
-            }
-            const float rsum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            const float alpha = m_new == m_run ? 1.f : ex2_approx(m_run - m_new);
             l_run = l_run * alpha + rsum;
-            m_run = m_use;
-            // warp-uniform: the TMEM round trip is .sync.aligned
-            const bool any_rescale = __any_sync(0xffffffffu, alpha != 1.f);
-            if (j >= 1 && any_rescale) {
-                // O is rescaled only once PV_{j-1} has finished accumulating
-                if (!warp_wait(&sm.bar_pv_done[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, sm, P.status)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t o_addr = tmem + lane_base + 128 * kSBuf + col0;
+            m_run = m_new;
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                // O_q holds PV_q(j-1) (complete: it was issued before S_q(j))
 #pragma unroll
-                for (int c4 = 0; c4 < 2; ++c4) {
+                for (int c4 = 0; c4 < 4; ++c4) {
                     uint32_t o[32];
-                    KVP_TMEM_LD32(o_addr + 32 * c4, o);
+                    KVP_TMEM_LD32(o_tm + 32 * c4, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int c = 0; c < 32; ++c)
                         o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                    KVP_TMEM_ST32(o_addr + 32 * c4, o);
+                    KVP_TMEM_ST32(o_tm + 32 * c4, o);
                 }
-                tmem_wait_st();
-            } else if (j >= 2) {
-                // P buffer j&1 was last read by PV_{j-2}
-                if (!warp_wait(&sm.bar_pv_done[j & 1], (uint32_t)((j - 2) >> 1) & 1u, sm, P.status)) { ok = false; break; }
             }
-            // P row half -> shared memory panel `half` of buffer j&1 (K-major, 128B swizzle).
-            uint8_t* pdst = sm.p[j & 1] + half * kPanel;
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                *reinterpret_cast<uint4*>(pdst + sw128_off(row, c)) =
-                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-            fence_proxy_async_smem();
+            // P -> the first 64 columns of S_q (bf16 pairs, key 2c in the low half)
+            KVP_TMEM_ST32(s_tm, pk);
+            KVP_TMEM_ST32(s_tm + 32, (pk + 32));
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&sm.bar_p_full[j & 1]);
+            mbar_arrive(&sm.bar_p_full[qt]);
         }
-        // Row sum = both halves' partial sums (same running max).
-        // (the max buffer of parity n_tiles&1 was last read two tiles ago)
-        float (&red_sum)[2][128] = sm.red[n_tiles & 1];
-        red_sum[half][row] = l_run;
-        mbar_arrive(&sm.bar_sum[rg]);
-        if (ok) ok = warp_wait(&sm.bar_sum[rg], 0, sm, P.status);
-        const float l_row = l_run + red_sum[half ^ 1][row];
-        if (ok && n_tiles > 0 &&
-            warp_wait(&sm.bar_pv_done[(n_tiles - 1) & 1], (uint32_t)((n_tiles - 1) >> 1) & 1u, sm, P.status)) {
+        if (ok && t.n_tiles > 0 && warp_wait(&sm.bar_o_done[qt], 0, sm, P.status)) {
             tc_fence_after();
-            const float inv = 1.f / l_row;
-            const uint32_t o_addr = tmem + lane_base + 128 * kSBuf + col0;
-            __nv_bfloat16* dst = P.out + (size_t)(w.q_row0 + row) * D + hcol + col0;
+            const float inv = 1.f / l_run;
+            __nv_bfloat16* dst = P.out + (size_t)(t.row0 + row) * D + hcol;
 #pragma unroll
-            for (int c4 = 0; c4 < 2; ++c4) {
+            for (int c4 = 0; c4 < 4; ++c4) {
                 uint32_t o[32];
-                KVP_TMEM_LD32(o_addr + 32 * c4, o);
+                KVP_TMEM_LD32(o_tm + 32 * c4, o);
                 tmem_wait_ld();
-                if (row < w.nq) {
+                if (row < t.nq) {
 #pragma unroll
                     for (int c = 0; c < 32; c += 8) {
                         uint4 pkt;
@@ -844,7 +987,9 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
     P.nheads = d.nheads;
     P.flat = d.flat;
     P.n_qt = (int)((T + kBM - 1) / kBM);
-    P.items_per_head = d.flat ? (int)((d.frames * T + kBM - 1) / kBM) : d.frames * P.n_qt;
+    P.n_pairs = (P.n_qt + kQTiles - 1) / kQTiles;
+    P.items_per_head = d.flat ? (int)(((long long)d.frames * T + kQTiles * kBM - 1) / (kQTiles * kBM))
+                              : d.frames * P.n_pairs;
     P.base_boxes = base_boxes;
     P.arena_boxes = arena_boxes;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)kDH);
@@ -856,6 +1001,17 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
         KVP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
         if (smem > optin) {
             set_error("attn_bf16: needs %d B of shared memory per block, device allows %d", smem, optin);
+            return KVP_ERR_UNSUPPORTED;
+        }
+    }
+    {
+        // setmaxnreg.inc waits until the warpgroup's registers exist in the
+        // CTA's pool: refuse a build whose launch pool is smaller than the split.
+        cudaFuncAttributes fa;
+        KVP_CUDA(cudaFuncGetAttributes(&fa, attn_bf16_sm100_kernel));
+        if ((long long)fa.numRegs * kThreads < (long long)kRegsLow * 128 + 2LL * kRegsHigh * 128) {
+            set_error("attn_bf16: kernel built with %d registers per thread, the register split needs %d",
+                      fa.numRegs, (kRegsLow * 128 + 2 * kRegsHigh * 128 + kThreads - 1) / kThreads);
             return KVP_ERR_UNSUPPORTED;
         }
     }
