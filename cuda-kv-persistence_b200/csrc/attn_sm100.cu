@@ -221,6 +221,59 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
+// One 128x128x128 GEMM as eight back-to-back K16 MMAs from a single asm
+// block: the descriptors of steps 1..7 are immediate offsets of step 0's, so
+// nothing but an add sits between two MMA issues and the tensor core's
+// shallow instruction queue never runs dry inside a GEMM.
+//   S = Q K^T: A and B K-major, 128B swizzle, two 64-column panels 16 KB
+//   apart: step ks starts (ks>>2)*16384 + (ks&3)*32 bytes in, i.e. adds
+//   (ks>>2)*1024 + (ks&3)*2 to the 16-byte address field.
+__device__ __forceinline__ void tc_gemm_ss(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred pf, pt;\n\t.reg .b64 a, b;\n\t"
+        "setp.ne.b32 pf, 0, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pf;\n\t"
+        "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
+        "add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
+        "add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
+        "add.s64 a, %1, 1024;\n\tadd.s64 b, %2, 1024;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
+        "add.s64 a, %1, 1026;\n\tadd.s64 b, %2, 1026;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
+        "add.s64 a, %1, 1028;\n\tadd.s64 b, %2, 1028;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
+        "add.s64 a, %1, 1030;\n\tadd.s64 b, %2, 1030;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t}"
+        ::"r"(d_tmem), "l"(a0), "l"(b0), "r"(idesc));
+}
+//   O (+)= P V: P from TMEM (step ks at column +8*ks), V MN-major with step
+//   ks 16 rows = 2048 bytes further (+128 in the address field).
+__device__ __forceinline__ void tc_gemm_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred pf, pt;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
+        "setp.ne.b32 pf, %4, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pf;\n\t"
+        "add.s32 a, %1, 8;\n\tadd.s64 b, %2, 128;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
+        "add.s32 a, %1, 16;\n\tadd.s64 b, %2, 256;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
+        "add.s32 a, %1, 24;\n\tadd.s64 b, %2, 384;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
+        "add.s32 a, %1, 32;\n\tadd.s64 b, %2, 512;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
+        "add.s32 a, %1, 40;\n\tadd.s64 b, %2, 640;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
+        "add.s32 a, %1, 48;\n\tadd.s64 b, %2, 768;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
+        "add.s32 a, %1, 56;\n\tadd.s64 b, %2, 896;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate));
+}
+
 #define KVP_TMEM_LD32(taddr, r)                                                                  \
     asm volatile(                                                                                \
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15," \
@@ -743,12 +796,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 }
                 const uint32_t q_s = smem_u32(sm.q[q]);
                 const uint32_t k_s = smem_u32(sm.k[sK]);
-#pragma unroll
-                for (int ks = 0; ks < kDH / 16; ++ks) {
-                    const uint32_t off = (uint32_t)(ks >> 2) * kPanel + (uint32_t)(ks & 3) * 32;
-                    tc_mma(tmem + 128u * q, sw128_desc(q_s + off, 16, 1024),
-                           sw128_desc(k_s + off, 16, 1024), idS, ks > 0 ? 1u : 0u);
-                }
+                tc_gemm_ss(tmem + 128u * q, sw128_desc(q_s, 16, 1024), sw128_desc(k_s, 16, 1024), idS);
                 tc_commit(&sm.bar_s_full[q]);
                 return true;
             };
@@ -758,11 +806,8 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 if (!mbar_wait(&sm.bar_p_full[q], (uint32_t)jv & 1u, sm, P.status)) return false;
                 tc_fence_after();
                 const uint32_t v_s = smem_u32(sm.v[sV]);
-#pragma unroll
-                for (int ks = 0; ks < kBN / 16; ++ks)
-                    tc_mma_ts(tmem + 256u + 128u * q, tmem + 128u * q + 8u * ks,
-                              sw128_desc(v_s + (uint32_t)ks * 2048, kPanel, 1024), idO,
-                              (jv > 0 || ks > 0) ? 1u : 0u);
+                tc_gemm_ts(tmem + 256u + 128u * q, tmem + 128u * q, sw128_desc(v_s, kPanel, 1024), idO,
+                           jv > 0 ? 1u : 0u);
                 if (jv == (q ? n1 : n0) - 1) tc_commit(&sm.bar_o_done[q]);
                 if (q == 1 || jv >= n1) tc_commit(&sm.bar_vempty[sV]);   // last reader of V_jv
                 return true;
