@@ -783,46 +783,67 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         // S_q(j) also covers PV_q(j-1): the softmax may rescale O_q as soon as
         // S_q(j) is visible.
         if (lane == 0) {
+            // A lean loop: the tensor core's instruction queue is shallow, so
+            // every cycle spent here between two GEMMs is a cycle it idles.
+            // Stage descriptors are precomputed (stage s of a ring is 32 KB =
+            // +2048 in the descriptor's 16-byte address field), stage indices
+            // and parities advance without division.
             constexpr uint32_t idS = idesc_bf16(false);
             constexpr uint32_t idO = idesc_bf16(true);
+            constexpr uint64_t kStageDesc = kTileBytes >> 4;
             const int n0 = w.t[0].n_tiles, n1 = w.t[1].n_tiles;
-            bool ok = true;
-            bool q_ready[kQTiles] = {false, false};
-            auto s_mma = [&](int q, int sK) -> bool {
-                if (!q_ready[q]) {
-                    if (!mbar_wait(&sm.bar_q[q], 0, sm, P.status)) return false;
-                    q_ready[q] = true;
-                    tc_fence_after();
-                }
-                const uint32_t q_s = smem_u32(sm.q[q]);
-                const uint32_t k_s = smem_u32(sm.k[sK]);
-                tc_gemm_ss(tmem + 128u * q, sw128_desc(q_s, 16, 1024), sw128_desc(k_s, 16, 1024), idS);
-                tc_commit(&sm.bar_s_full[q]);
-                return true;
-            };
-            auto pv_mma = [&](int q, int jv) -> bool {
-                const int sV = jv % kVStages;
-                if (!mbar_wait(&sm.bar_vfull[sV], (uint32_t)(jv / kVStages) & 1u, sm, P.status)) return false;
-                if (!mbar_wait(&sm.bar_p_full[q], (uint32_t)jv & 1u, sm, P.status)) return false;
-                tc_fence_after();
-                const uint32_t v_s = smem_u32(sm.v[sV]);
-                tc_gemm_ts(tmem + 256u + 128u * q, tmem + 128u * q, sw128_desc(v_s, kPanel, 1024), idO,
-                           jv > 0 ? 1u : 0u);
-                if (jv == (q ? n1 : n0) - 1) tc_commit(&sm.bar_o_done[q]);
-                if (q == 1 || jv >= n1) tc_commit(&sm.bar_vempty[sV]);   // last reader of V_jv
-                return true;
-            };
+            const uint64_t dq0 = sw128_desc(smem_u32(sm.q[0]), 16, 1024);
+            const uint64_t dq1 = sw128_desc(smem_u32(sm.q[1]), 16, 1024);
+            const uint64_t dk = sw128_desc(smem_u32(sm.k[0]), 16, 1024);
+            const uint64_t dv = sw128_desc(smem_u32(sm.v[0]), kPanel, 1024);
+            const uint32_t s0_tm = tmem, s1_tm = tmem + 128u, o0_tm = tmem + 256u, o1_tm = tmem + 384u;
+            bool ok = n_tiles == 0 || mbar_wait(&sm.bar_q[0], 0, sm, P.status);
+            if (ok && n1 > 0) ok = mbar_wait(&sm.bar_q[1], 0, sm, P.status);
+            uint32_t ks = 0, kph = 0;          // K ring stage / parity of tile j
+            uint32_t vs = 0, vph = 0;          // V ring stage / parity of tile j
+            uint32_t pvs = 0, pvph = 0;        // ... of tile j-1
             for (int j = 0; ok && j < n_tiles; ++j) {
-                const int sK = j % kKStages;
-                if (!mbar_wait(&sm.bar_kfull[sK], (uint32_t)(j / kKStages) & 1u, sm, P.status)) { ok = false; break; }
+                if (!mbar_wait(&sm.bar_kfull[ks], kph, sm, P.status)) { ok = false; break; }
                 tc_fence_after();
-                if (j < n0 && !s_mma(0, sK)) { ok = false; break; }
-                if (j >= 1 && j - 1 < n1 && !pv_mma(1, j - 1)) { ok = false; break; }
-                if (j < n1 && !s_mma(1, sK)) { ok = false; break; }
-                tc_commit(&sm.bar_kempty[sK]);
-                if (j < n0 && !pv_mma(0, j)) { ok = false; break; }
+                if (j < n0) {
+                    tc_gemm_ss(s0_tm, dq0, dk + ks * kStageDesc, idS);
+                    tc_commit(&sm.bar_s_full[0]);
+                }
+                if (j >= 1 && j - 1 < n1) {    // PV1(j-1)
+                    if (j - 1 >= n0 && !mbar_wait(&sm.bar_vfull[pvs], pvph, sm, P.status)) { ok = false; break; }
+                    if (!mbar_wait(&sm.bar_p_full[1], (uint32_t)(j - 1) & 1u, sm, P.status)) { ok = false; break; }
+                    tc_fence_after();
+                    tc_gemm_ts(o1_tm, s1_tm, dv + pvs * kStageDesc, idO, j > 1 ? 1u : 0u);
+                    if (j == n1) tc_commit(&sm.bar_o_done[1]);
+                    tc_commit(&sm.bar_vempty[pvs]);
+                }
+                if (j < n1) {
+                    tc_gemm_ss(s1_tm, dq1, dk + ks * kStageDesc, idS);
+                    tc_commit(&sm.bar_s_full[1]);
+                }
+                tc_commit(&sm.bar_kempty[ks]);
+                if (j < n0) {                  // PV0(j)
+                    if (!mbar_wait(&sm.bar_vfull[vs], vph, sm, P.status)) { ok = false; break; }
+                    if (!mbar_wait(&sm.bar_p_full[0], (uint32_t)j & 1u, sm, P.status)) { ok = false; break; }
+                    tc_fence_after();
+                    tc_gemm_ts(o0_tm, s0_tm, dv + vs * kStageDesc, idO, j > 0 ? 1u : 0u);
+                    if (j == n0 - 1) tc_commit(&sm.bar_o_done[0]);
+                    if (j >= n1) tc_commit(&sm.bar_vempty[vs]);   // no PV1 reads V(j)
+                }
+                pvs = vs; pvph = vph;
+                if (++vs == kVStages) { vs = 0; vph ^= 1u; }
+                if (++ks == kKStages) { ks = 0; kph ^= 1u; }
             }
-            if (ok && n_tiles > 0 && n_tiles - 1 < n1) pv_mma(1, n_tiles - 1);
+            if (ok && n_tiles > 0 && n_tiles - 1 < n1) {   // PV1(last)
+                const int jl = n_tiles - 1;
+                if ((jl < n0 || mbar_wait(&sm.bar_vfull[pvs], pvph, sm, P.status)) &&
+                    mbar_wait(&sm.bar_p_full[1], (uint32_t)jl & 1u, sm, P.status)) {
+                    tc_fence_after();
+                    tc_gemm_ts(o1_tm, s1_tm, dv + pvs * kStageDesc, idO, jl > 0 ? 1u : 0u);
+                    tc_commit(&sm.bar_o_done[1]);
+                    tc_commit(&sm.bar_vempty[pvs]);
+                }
+            }
             // Drain: every issued MMA lands before TMEM is freed.
             tc_commit(&sm.bar_mma_done);
             const unsigned long long t0 = globaltimer();
