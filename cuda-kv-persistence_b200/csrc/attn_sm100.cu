@@ -295,6 +295,20 @@ __device__ __forceinline__ void tc_gemm_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),        \
         "r"(r[29]), "r"(r[30]), "r"(r[31]) : "memory")
 
+// tcgen05.wait::ld that also names the 32 destination registers of the
+// load in flight as in/out operands, so no use of them can be scheduled
+// before the wait (the load writes them asynchronously).
+#define KVP_TMEM_WAIT_LD_DEP(r)                                                                   \
+    asm volatile("tcgen05.wait::ld.sync.aligned;"                                                \
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),        \
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),      \
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),  \
+                   "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),  \
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),  \
+                   "+r"(r[30]), "+r"(r[31])                                                       \
+                 :                                                                                \
+                 : "memory")
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -476,9 +490,9 @@ __device__ __forceinline__ Work decode_work(const Params& P) {
 // ----------------------------------------------------------- softmax pieces
 // One S row (this thread's TMEM lane, 128 columns) -> P = 2^(s*sl2 - m) as
 // packed bf16 pairs in pk, returns the fp32 row sum of P.  Columns at or
-// past `left` are masked (-inf) when kMask.  A quarter of the exponentials
-// run on the FMA pipe (ex2_poly2), the rest on MUFU; scaling and the row sum
-// use f32x2 arithmetic.
+// past `left` are masked (-inf) when kMask.  One exponential in eight runs
+// on the FMA pipe (ex2_poly2), the rest on MUFU; scaling and the row sum use
+// f32x2 arithmetic.
 template <bool kMask>
 __device__ __forceinline__ float exp_row(uint32_t s_addr, float m, float sl2, int left, uint32_t (&pk)[64]) {
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
@@ -486,22 +500,27 @@ __device__ __forceinline__ float exp_row(uint32_t s_addr, float m, float sl2, in
     uint64_t acc[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i] = 0ull;   // (+0, +0)
+    // 32-column chunks, software-pipelined: chunk h+1 is loading from TMEM
+    // while chunk h is computed.
+    uint32_t sa[32], sb[32];
+    KVP_TMEM_LD32(s_addr, sa);
+    KVP_TMEM_WAIT_LD_DEP(sa);
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-        uint32_t sr[32];
-        KVP_TMEM_LD32(s_addr + 32 * h, sr);
-        tmem_wait_ld();
+        uint32_t(&cur)[32] = (h & 1) ? sb : sa;
+        uint32_t(&nxt)[32] = (h & 1) ? sa : sb;
+        if (h < 3) KVP_TMEM_LD32(s_addr + 32 * (h + 1), nxt);
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-            float s0 = __uint_as_float(sr[c]);
-            float s1 = __uint_as_float(sr[c + 1]);
+            float s0 = __uint_as_float(cur[c]);
+            float s1 = __uint_as_float(cur[c + 1]);
             if (kMask) {
                 if (32 * h + c >= left) s0 = -INFINITY;
                 if (32 * h + c + 1 >= left) s1 = -INFINITY;
             }
             float x0, x1, p0, p1;
             f2_unpack(f2_fma(f2_pack(s0, s1), sl2x2, negm2), x0, x1);
-            if ((c & 7) == 6) {
+            if ((c & 15) == 14) {   // one pair in eight on the FMA pipe
                 ex2_poly2(x0, x1, p0, p1);
             } else {
                 p0 = ex2_approx(x0);
@@ -510,6 +529,7 @@ __device__ __forceinline__ float exp_row(uint32_t s_addr, float m, float sl2, in
             acc[(c >> 1) & 3] = f2_add(acc[(c >> 1) & 3], f2_pack(p0, p1));
             pk[16 * h + (c >> 1)] = pack_bf16(p0, p1);
         }
+        if (h < 3) KVP_TMEM_WAIT_LD_DEP(nxt);
     }
     const uint64_t a2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
     float lo, hi;
