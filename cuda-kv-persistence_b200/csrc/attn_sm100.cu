@@ -559,6 +559,14 @@ __device__ __forceinline__ float max_row(uint32_t s_addr, int left) {
                  fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
 }
 
+// Stage release by the softmax: valid when the tile issuing
+// the last S GEMM of every K/V step also issues the PV GEMMs of the step
+// before it -- Q1 when it has the full key span (n1 == max), or Q0 alone.
+// The only other case, 0 < n1 < n0, does not arise from decode_work (flat
+// tiles have n1 >= n0, per-frame tiles n1 in {0, n0}); the MMA issuer then
+// releases the stages itself.
+__device__ __forceinline__ bool soft_release(int n0, int n1) { return !(n1 > 0 && n1 < n0); }
+
 // ------------------------------------------------------------------ kernel
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_constant__ Params P) {
@@ -817,6 +825,10 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             const uint64_t dk = sw128_desc(smem_u32(sm.k[0]), 16, 1024);
             const uint64_t dv = sw128_desc(smem_u32(sm.v[0]), kPanel, 1024);
             const uint32_t s0_tm = tmem, s1_tm = tmem + 128u, o0_tm = tmem + 256u, o1_tm = tmem + 384u;
+            // K/V stages are released by the softmax warpgroup that sees the
+            // tile's last S GEMM land (see soft_release); only the tile
+            // counts that never occur in practice fall back to commits here.
+            const bool own_release = !soft_release(n0, n1);
             bool ok = n_tiles == 0 || mbar_wait(&sm.bar_q[0], 0, sm, P.status);
             if (ok && n1 > 0) ok = mbar_wait(&sm.bar_q[1], 0, sm, P.status);
             uint32_t ks = 0, kph = 0;          // K ring stage / parity of tile j
@@ -835,20 +847,20 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     tc_fence_after();
                     tc_gemm_ts(o1_tm, s1_tm, dv + pvs * kStageDesc, idO, j > 1 ? 1u : 0u);
                     if (j == n1) tc_commit(&sm.bar_o_done[1]);
-                    tc_commit(&sm.bar_vempty[pvs]);
+                    if (own_release) tc_commit(&sm.bar_vempty[pvs]);
                 }
                 if (j < n1) {
                     tc_gemm_ss(s1_tm, dq1, dk + ks * kStageDesc, idS);
                     tc_commit(&sm.bar_s_full[1]);
                 }
-                tc_commit(&sm.bar_kempty[ks]);
+                if (own_release) tc_commit(&sm.bar_kempty[ks]);
                 if (j < n0) {                  // PV0(j)
                     if (!mbar_wait(&sm.bar_vfull[vs], vph, sm, P.status)) { ok = false; break; }
                     if (!mbar_wait(&sm.bar_p_full[0], (uint32_t)j & 1u, sm, P.status)) { ok = false; break; }
                     tc_fence_after();
                     tc_gemm_ts(o0_tm, s0_tm, dv + vs * kStageDesc, idO, j > 0 ? 1u : 0u);
                     if (j == n0 - 1) tc_commit(&sm.bar_o_done[0]);
-                    if (j >= n1) tc_commit(&sm.bar_vempty[vs]);   // no PV1 reads V(j)
+                    if (own_release && j >= n1) tc_commit(&sm.bar_vempty[vs]);   // no PV1 reads V(j)
                 }
                 pvs = vs; pvph = vph;
                 if (++vs == kVStages) { vs = 0; vph ^= 1u; }
@@ -861,7 +873,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     tc_fence_after();
                     tc_gemm_ts(o1_tm, s1_tm, dv + pvs * kStageDesc, idO, jl > 0 ? 1u : 0u);
                     tc_commit(&sm.bar_o_done[1]);
-                    tc_commit(&sm.bar_vempty[pvs]);
+                    if (own_release) tc_commit(&sm.bar_vempty[pvs]);
                 }
             }
             // Drain: every issued MMA lands before TMEM is freed.
@@ -885,9 +897,19 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         const float sl2 = P.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;          // m in log2 units, scaled
         bool ok = true;
+        // The warpgroup of the tile whose S GEMM comes last in each K/V step
+        // releases the stages: S_q(j) landing means every MMA issued before
+        // it has landed too, i.e. K(j) (both S GEMMs) and V(j-1) (both PV
+        // GEMMs) are no longer read.
+        const bool releaser = soft_release(w.t[0].n_tiles, w.t[1].n_tiles) &&
+                              qt == (w.t[1].n_tiles > 0 ? 1 : 0) && (warp & 3) == 0 && lane == 0;
         for (int j = 0; j < t.n_tiles; ++j) {
             if (!warp_wait(&sm.bar_s_full[qt], (uint32_t)j & 1u, sm, P.status)) { ok = false; break; }
             tc_fence_after();
+            if (releaser) {
+                mbar_arrive(&sm.bar_kempty[j % kKStages]);
+                if (j > 0) mbar_arrive(&sm.bar_vempty[(j - 1) % kVStages]);
+            }
             const long long left_ll = my_khi - (w.klo + (long long)j * kBN);
             const int left = left_ll >= kBN ? kBN : (left_ll < 0 ? 0 : (int)left_ll);
             const bool masked = !__all_sync(0xffffffffu, left == kBN);
