@@ -430,6 +430,22 @@ def run_e2e(args, stack, scores, dev, stream, world, local_rank):
             "path": "kvp Session + kvp_attn_bf16 C ABI, pinned host Q/K/V/O per layer chunk"}
 
 
+def run_matrix(args) -> int:
+    """Per-frame cross-attention measurements (kvp/matrix.py), 1 GPU."""
+    import torch
+    from kvp import matrix
+    torch.cuda.set_device(0)
+    if args.matrix == 5:
+        for row in matrix.run_config5(reps=max(1, args.reps), seed=args.seed,
+                                      streaming=args.streaming):
+            print(json.dumps({"metric": "config5 cell", "streaming": args.streaming, **row}),
+                  flush=True)
+    else:
+        print(json.dumps({"metric": "config2", **matrix.run_config2(reps=max(1, args.reps),
+                                                                   seed=args.seed)}), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -447,7 +463,16 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--matrix", type=int, choices=[2, 5], default=0,
+                    help="instead of the config-4 line: config 5 (policy x budget x regime, one "
+                         "JSON line per cell) or config 2 (one line), per-frame cross attention")
+    ap.add_argument("--reps", type=int, default=3, help="repetitions per cell with --matrix (ABBA)")
+    ap.add_argument("--streaming", action="store_true",
+                    help="with --matrix 5: streaming arena (sticky slots, LIFO reuse) instead of "
+                         "re-staging every admitted row every frame")
     args = ap.parse_args()
+    if args.matrix:
+        return run_matrix(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -186,6 +186,15 @@ __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t parity, Smem& sm
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// 16-byte global -> shared copy (L2 only), zero-filling the bytes past
+// src_bytes (0 or 16).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
     asm volatile(
@@ -748,7 +757,9 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     }
                 }
                 // Mixed / padding groups: lane -> (panel = lane/16, row = (lane/2)%8,
-                // chunks 4*(lane%2) .. +3); 16-byte copies into the swizzled layout.
+                // chunks 4*(lane%2) .. +3); one 16-byte cp.async per chunk into the
+                // swizzled layout (zero-filled for padding rows), every group of
+                // the tile in flight at once, then one wait.
                 unsigned mm = mixed_mask & 0x55555555u;
                 const int pnl = lane >> 4, rr = (lane >> 1) & 7, c0 = 4 * (lane & 1);
                 while (mm) {
@@ -765,22 +776,23 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     const long long m_row = sel == 0 ? e0 : sel == 1 ? e1 : sel == 2 ? e2 : e3;
                     const long long key = r0 + row_in_tile;
                     const bool is_pad = key >= w.khi;
-                    const __nv_bfloat16* src = m_row >= 0
-                        ? P.arena + (size_t)m_row * 2 * D + acol + 64 * pnl
-                        : base + (size_t)key * D + hcol + 64 * pnl;
-                    uint4 buf[4];
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        buf[c] = is_pad ? make_uint4(0, 0, 0, 0)
-                                        : __ldg(reinterpret_cast<const uint4*>(src) + c0 + c);
+                    // (a padding row reads nothing; its source is any valid address)
+                    const __nv_bfloat16* src = is_pad ? base
+                        : m_row >= 0 ? P.arena + (size_t)m_row * 2 * D + acol + 64 * pnl
+                                     : base + (size_t)key * D + hcol + 64 * pnl;
                     uint8_t* dst = dst_tile + pnl * kPanel;
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
-                        *reinterpret_cast<uint4*>(dst + sw128_off(row_in_tile, c0 + c)) = buf[c];
+                        cp_async16(dst + sw128_off(row_in_tile, c0 + c),
+                                   reinterpret_cast<const uint4*>(src) + (is_pad ? 0 : c0 + c),
+                                   is_pad ? 0u : 16u);
                 }
-                // make the warp's own stores visible to the tensor cores (only
-                // when some group was copied by hand)
-                if (mixed_mask & 0x55555555u) fence_proxy_async_smem();
+                // the copies have landed; make them visible to the tensor cores
+                // (only when some group was copied by hand)
+                if (mixed_mask & 0x55555555u) {
+                    cp_async_wait_all();
+                    fence_proxy_async_smem();
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(full);

@@ -1,0 +1,168 @@
+"""Per-frame cross-attention workloads: BASELINE config 5 (policy x budget x
+motion regime) and config 2 (8-frame cross, Recency).
+
+One cell is the reference driver's per-frame loop
+(src/run_policy_experiment.cu:156-274) for F frames x T tokens, one layer of
+H heads, bf16: for every frame f the Session selects, releases and stages the
+admitted tiles' rows into the arena, uploads the KVMap, sets the persisting
+window over the arena, and the tcgen05 kernel runs query frame f over key
+frames 0..f.  Everything is issued on one stream; unlike the reference there
+is no device synchronisation per frame.
+
+`cell_order` fixes the order of the cells (regime, budget, policy) and the
+repetition order: forward, then backward (ABBA), as the reference's variance
+test does (tests/test_variance.py:141-147).  The DRAM bytes of a cell come
+from an ncu pass over one repetition (`--metrics dram__bytes_read.sum,...`):
+each cell launches exactly `frames` attention kernels, in cell order.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .attention import attn_bf16, read_status
+from .session import Session
+from .traces import motion_config2, motion_config5, qkv
+
+POLICY_ORDER = ("none", "uniform", "recency", "motion", "reuse_weighted")
+BUDGET_FRACS = (0.10, 0.25, 0.50, 1.00)
+REGIMES = ("static", "high")
+
+
+@dataclass
+class Cell:
+    regime: str
+    budget_frac: float
+    policy: str
+
+
+def cell_order() -> list[Cell]:
+    return [Cell(r, b, p) for r in REGIMES for b in BUDGET_FRACS for p in POLICY_ORDER]
+
+
+def cross_flops(frames: int, tokens: int, heads: int, head_dim: int = 128) -> float:
+    """4 * T_q * S * head_dim per (frame, head), S = (f+1)*T keys."""
+    return float(sum(4 * tokens * (f + 1) * tokens * head_dim for f in range(frames)) * heads)
+
+
+def run_frames(q, k, v, out, scores, *, policy: str, set_aside: int, frames: int, tokens: int,
+               heads: int, stream: int, streaming: bool = False, events=None) -> dict:
+    """One pass over all frames of a cell.  The Session (device buffers) is
+    created before and destroyed after the optional (start, end) CUDA events,
+    so a timed pass holds only the per-frame work."""
+    hidden = heads * 128
+    s = Session(mode="cross", policy=policy, frames=frames, tokens=tokens, hidden=hidden,
+                elem_bytes=2, set_aside=set_aside, streaming=streaming, layers=1)
+    copies = staged = 0
+    try:
+        if events:
+            events[0].record()
+        for f in range(frames):
+            st = s.plan_frame(f, scores)
+            copies += st.copies
+            staged += st.staged_bytes
+            if policy != "none":
+                s.upload(stream)
+                s.stage([k.data_ptr()], [v.data_ptr()], stream)
+                s.window(0, stream)
+                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
+                          mode="causal", kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(0),
+                          arena_rows=s.cap_rows, stream=stream)
+            else:
+                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
+                          mode="causal", stream=stream)
+        if policy != "none":
+            s.clear_window(stream)
+        if events:
+            events[1].record()
+        torch.cuda.synchronize()   # the Session's buffers outlive every launch
+        s.finish()
+    finally:
+        s.close()
+    return {"copies": copies, "staged_bytes": staged}
+
+
+def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: int = 12,
+                seed: int = 0, max_persist: int | None = None, streaming: bool = False,
+                device="cuda") -> list[dict]:
+    """All 40 cells, `reps` repetitions each in ABBA order; one dict per cell."""
+    from ._lib import DeviceInfo, lib
+    import ctypes as C
+    if max_persist is None:
+        info = DeviceInfo()
+        lib().kvp_query_device(-1, C.byref(info))
+        max_persist = int(info.max_persisting_l2_bytes)
+    hidden = heads * 128
+    rows = frames * tokens
+    q, k, v = (t.to(device) for t in qkv(rows, hidden, seed=seed))
+    out = torch.empty_like(q)
+    ref = torch.empty_like(q)
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    flops = cross_flops(frames, tokens, heads)
+    cells = cell_order()
+    scores = {r: motion_config5(r, frames=frames, seed=seed) for r in REGIMES}
+    times = {i: [] for i in range(len(cells))}
+    counters = {}
+    read_status()
+    # warm-up pass over every cell (also the bitwise check against None)
+    for i, c in enumerate(cells):
+        counters[i] = run_frames(q, k, v, out, scores[c.regime], policy=c.policy,
+                                 set_aside=int(c.budget_frac * max_persist), frames=frames,
+                                 tokens=tokens, heads=heads, stream=stream, streaming=streaming)
+        if c.policy == "none":
+            ref.copy_(out)
+        elif not torch.equal(out, ref):
+            raise RuntimeError(f"cell {c} differs from the None policy")
+    order = []
+    for r in range(reps):
+        seq = list(range(len(cells)))
+        order += seq if r % 2 == 0 else seq[::-1]
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    for i in order:
+        c = cells[i]
+        run_frames(q, k, v, out, scores[c.regime], policy=c.policy,
+                   set_aside=int(c.budget_frac * max_persist), frames=frames, tokens=tokens,
+                   heads=heads, stream=stream, streaming=streaming, events=(e0, e1))
+        times[i].append(e0.elapsed_time(e1))
+    status = read_status()
+    res = []
+    for i, c in enumerate(cells):
+        t = np.array(times[i])
+        res.append({"regime": c.regime, "budget_frac": c.budget_frac,
+                    "set_aside_bytes": int(c.budget_frac * max_persist), "policy": c.policy,
+                    "ms_mean": round(float(t.mean()), 4), "ms_std": round(float(t.std(ddof=1)) if len(t) > 1 else 0.0, 4),
+                    "cv_pct": round(float(100 * t.std(ddof=1) / t.mean()) if len(t) > 1 else 0.0, 3),
+                    "tflops": round(flops / (t.mean() / 1e3) / 1e12, 2), "reps": len(t),
+                    "copies_per_pass": counters[i]["copies"],
+                    "staged_bytes_per_pass": counters[i]["staged_bytes"], "device_status": status})
+    return res
+
+
+def run_config2(*, reps: int = 3, frames: int = 8, tokens: int = 1560, heads: int = 12,
+                seed: int = 0, tiles: int = 22, device="cuda") -> dict:
+    """Config 2: 8 frames cross, AR(1) motion, Recency with 22 tiles (bf16 budget)."""
+    hidden = heads * 128
+    rows = frames * tokens
+    q, k, v = (t.to(device) for t in qkv(rows, hidden, seed=seed))
+    out = torch.empty_like(q)
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    scores = motion_config2(frames=frames, seed=seed)
+    set_aside = tiles * 16 * hidden * 2 * 2
+    read_status()
+    run_frames(q, k, v, out, scores, policy="recency", set_aside=set_aside, frames=frames,
+               tokens=tokens, heads=heads, stream=stream)
+    ts = []
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    for _ in range(reps):
+        run_frames(q, k, v, out, scores, policy="recency", set_aside=set_aside, frames=frames,
+                   tokens=tokens, heads=heads, stream=stream, events=(e0, e1))
+        ts.append(e0.elapsed_time(e1))
+    t = float(np.mean(ts))
+    return {"config": 2, "policy": "recency", "tiles": tiles, "frames": frames,
+            "ms_mean": round(t, 4), "tflops": round(cross_flops(frames, tokens, heads) / (t / 1e3) / 1e12, 2),
+            "device_status": read_status()}

@@ -1,0 +1,28 @@
+"""Host-side checks of the per-frame cross-attention harness (kvp/matrix.py)."""
+
+from __future__ import annotations
+
+import pytest
+
+
+def test_config5_cells_and_flops():
+    from kvp import matrix
+    cells = matrix.cell_order()
+    assert len(cells) == 5 * 4 * 2
+    assert {c.policy for c in cells} == {"none", "uniform", "recency", "motion", "reuse_weighted"}
+    # None leads every (regime, budget) group: the other policies are checked against it
+    for i in range(0, len(cells), 5):
+        assert cells[i].policy == "none"
+        assert len({(c.regime, c.budget_frac) for c in cells[i:i + 5]}) == 1
+    # 16 frames x 1560 tokens x 12 heads: 2.0335e12 FLOP per cell
+    assert matrix.cross_flops(16, 1560, 12) == pytest.approx(2.0335e12, rel=1e-4)
+    # config 2: 8 frames
+    assert matrix.cross_flops(8, 1560, 12) == pytest.approx(5.383e11, rel=1e-3)
+
+
+def test_config5_regimes_shapes():
+    from kvp.traces import motion_config5
+    s = motion_config5("static", frames=16)
+    h = motion_config5("high", frames=16)
+    assert s.shape == h.shape == (16, 98)
+    assert s.max() < 0.05 and h.max() < 1.0 and h.max() > 0.5
