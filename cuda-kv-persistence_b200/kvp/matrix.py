@@ -1,5 +1,6 @@
 """Per-frame cross-attention workloads: BASELINE config 5 (policy x budget x
-motion regime) and config 2 (8-frame cross, Recency).
+motion regime), config 2 (8-frame cross, Recency) and config 3 (50-frame
+trace, 30 layers, 5-frame causal window, ReuseWeighted).
 
 One cell is the reference driver's per-frame loop
 (src/run_policy_experiment.cu:156-274) for F frames x T tokens, one layer of
@@ -25,7 +26,7 @@ import torch
 
 from .attention import attn_bf16, read_status
 from .session import Session
-from .traces import motion_config2, motion_config5, qkv
+from .traces import motion_config2, motion_config3, motion_config5, qkv
 
 POLICY_ORDER = ("none", "uniform", "recency", "motion", "reuse_weighted")
 BUDGET_FRACS = (0.10, 0.25, 0.50, 1.00)
@@ -166,3 +167,94 @@ def run_config2(*, reps: int = 3, frames: int = 8, tokens: int = 1560, heads: in
     return {"config": 2, "policy": "recency", "tiles": tiles, "frames": frames,
             "ms_mean": round(t, 4), "tflops": round(cross_flops(frames, tokens, heads) / (t / 1e3) / 1e12, 2),
             "device_status": read_status()}
+
+
+def window_flops(frames: int, tokens: int, heads: int, layers: int, window: int,
+                 head_dim: int = 128) -> float:
+    """4 * T_q * S * head_dim per (frame, head, layer), S = min(f+1, window)*T keys."""
+    units = sum(min(f + 1, window) for f in range(frames))
+    return float(4 * tokens * tokens * head_dim * units * heads * layers)
+
+
+def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: int = 12,
+                layers: int = 30, window: int = 5, seed: int = 0, streaming: bool = False,
+                device="cuda") -> list[dict]:
+    """Config 3: per frame one admission (ReuseWeighted over the window's
+    tiles, budget = the device's max persisting L2), the admitted rows staged
+    into every layer's arena with one launch, then per layer the persisting
+    window over its arena and one attention launch (query frame f, key frames
+    max(0, f-window+1)..f).  Also the None policy on the same inputs."""
+    from ._lib import DeviceInfo, lib
+    import ctypes as C
+    info = DeviceInfo()
+    lib().kvp_query_device(-1, C.byref(info))
+    budget = int(info.max_persisting_l2_bytes)
+    hidden = heads * 128
+    rows = frames * tokens
+    qs, ks, vs = [], [], []
+    for layer in range(layers):
+        q, k, v = qkv(rows, hidden, seed=seed * 1000 + layer, device=device)
+        qs.append(q); ks.append(k); vs.append(v)
+    outs = [torch.empty_like(qs[0]) for _ in range(layers)]
+    refs = None
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    scores = motion_config3(frames=frames, seed=seed)
+    flops = window_flops(frames, tokens, heads, layers, window)
+
+    def one_pass(policy, events=None):
+        s = Session(mode="cross", policy=policy, frames=frames, tokens=tokens, hidden=hidden,
+                    elem_bytes=2, set_aside=budget, window=window, layers=layers,
+                    streaming=streaming)
+        try:
+            if events:
+                events[0].record()
+            for f in range(frames):
+                s.plan_frame(f, scores)
+                persist = policy != "none"
+                if persist:
+                    s.upload(stream)
+                    s.stage([t.data_ptr() for t in ks], [t.data_ptr() for t in vs], stream)
+                for layer in range(layers):
+                    if persist:
+                        s.window(layer, stream)
+                        attn_bf16(qs[layer], ks[layer], vs[layer], outs[layer], tokens=tokens,
+                                  frames=1, q_frame0=f, heads=heads, mode="causal", window=window,
+                                  kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(layer),
+                                  arena_rows=s.cap_rows, stream=stream)
+                    else:
+                        attn_bf16(qs[layer], ks[layer], vs[layer], outs[layer], tokens=tokens,
+                                  frames=1, q_frame0=f, heads=heads, mode="causal", window=window,
+                                  stream=stream)
+            if policy != "none":
+                s.clear_window(stream)
+            if events:
+                events[1].record()
+            torch.cuda.synchronize()
+            s.finish()
+        finally:
+            s.close()
+
+    read_status()
+    res = []
+    for policy in ("none", "reuse_weighted"):
+        one_pass(policy)   # warm-up
+        if policy == "none":
+            refs = [o.clone() for o in outs]
+        else:
+            for a, b in zip(outs, refs):
+                if not torch.equal(a, b):
+                    raise RuntimeError("config 3: ReuseWeighted output differs from None")
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        ts = []
+        for _ in range(max(1, reps)):
+            one_pass(policy, (e0, e1))
+            ts.append(e0.elapsed_time(e1))
+        t = float(np.mean(ts))
+        res.append({"config": 3, "policy": policy, "streaming": streaming, "frames": frames,
+                    "layers": layers,
+                    "window": window, "set_aside_bytes": budget, "ms_mean": round(t, 3),
+                    "ms_runs": [round(x, 3) for x in ts],
+                    "tflops": round(flops / (t / 1e3) / 1e12, 2), "flop": flops,
+                    "device_status": read_status()})
+    return res

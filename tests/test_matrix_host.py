@@ -26,3 +26,10 @@ def test_config5_regimes_shapes():
     h = motion_config5("high", frames=16)
     assert s.shape == h.shape == (16, 98)
     assert s.max() < 0.05 and h.max() < 1.0 and h.max() > 0.5
+
+
+def test_config3_flops():
+    from kvp import matrix
+    # 50 frames, window of 5 frames: 240 frame-units per (layer, head); 1.0765e14 FLOP
+    assert matrix.window_flops(50, 1560, 12, 30, 5) == pytest.approx(1.0765e14, rel=1e-4)
+    assert matrix.window_flops(3, 1560, 12, 1, 5) == pytest.approx(matrix.cross_flops(3, 1560, 12))
