@@ -18,11 +18,14 @@
 //               (all base / one ascending arena run / mixed) and stages the
 //               tile with TMA boxes (one 128-row box per panel when the whole
 //               tile is base rows, power-of-two boxes per run otherwise);
-//               mixed groups and padding are copied with 16-byte loads into
-//               the same 128B-swizzled layout
+//               mixed groups and padding are copied with 16-byte cp.async
+//               into the same 128B-swizzled layout
 //   warp 1      TMEM allocation and the single-thread MMA issuer, in the
 //               order S0_j, PV1_{j-1}, S1_j, PV0_j: while one tile's softmax
-//               runs, the tensor cores work on the other tile
+//               runs, the tensor cores work on the other tile.  Each GEMM is
+//               one asm block of eight MMAs.
+//   warp 3      idle (its warpgroup gives registers to the softmax:
+//               setmaxnreg 104 / 200)
 //   warps 4-7   softmax of Q0, warps 8-11 softmax of Q1: thread i owns query
 //               row i (TMEM lane i) and all 128 columns of each S tile.
 //               Exponentials are computed with the running max first; only a
@@ -30,7 +33,9 @@
 //               log2 units) recomputes with the new max and rescales O.  P is
 //               written back into the first 64 columns of its own S
 //               accumulator as packed bf16 and read from there by the PV MMA.
-//               The same warps run the epilogue O / l -> bf16 -> global.
+//               The warpgroup of the tile with the full key span also
+//               releases the K/V stages once its S tile lands.  The same
+//               warps run the epilogue O / l -> bf16 -> global.
 // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512).
 // Shared memory: Q0, Q1 (32 KB each), a K ring of two and a V ring of three
 // 32 KB stages.  Every mbarrier wait is bounded (about one second of

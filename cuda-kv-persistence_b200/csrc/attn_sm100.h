@@ -29,7 +29,7 @@ struct LayerIO {
 //   mode 0 (intra): frame f's keys are rows [f*T, (f+1)*T);
 //   mode 1 (causal): frame f's keys are rows [b*T, (f+1)*T) with
 //        b = window ? max(0, f-window+1) : 0;
-//   flat = 1 (causal, no window): 128-row query tiles run across frame
+//   flat = 1 (causal, no window): query tiles run across frame
 //        boundaries, each row masked at its own frame's limit (no padding
 //        work at the 1560 = 12*128 + 24 frame tail).
 struct AttnDesc {
