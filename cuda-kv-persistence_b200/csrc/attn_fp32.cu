@@ -210,12 +210,13 @@ int launch_attn_fp32(const float* q, const float* k, const float* v, const float
         set_error("attn_fp32: Q/K/V/Out/Arena must be 16-byte aligned");
         return KVP_ERR_ARG;
     }
-    static bool attr_set = false;
     const int smem = (int)sizeof(Fp32Smem);
-    if (!attr_set) {
+    static PerDeviceOnce setup;
+    const int rc_setup = setup([&](int) -> int {
         KVP_CUDA(cudaFuncSetAttribute(attn_fp32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr_set = true;
-    }
+        return KVP_OK;
+    });
+    if (rc_setup != KVP_OK) return rc_setup;
     dim3 grid((unsigned)((T + kBQ - 1) / kBQ), (unsigned)heads, (unsigned)frames);
     attn_fp32_kernel<<<grid, kThreads, smem, stream>>>(q, k, v, arena, kvmap, out, T, D, k_lo, k_hi,
                                                        arena_rows, frame_stride_rows, d_status);

@@ -1120,16 +1120,14 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)kDH);
 
     const int smem = (int)sizeof(Smem);
-    {
-        int dev = 0, optin = 0;
-        KVP_CUDA(cudaGetDevice(&dev));
+    static PerDeviceOnce setup;
+    const int rc_setup = setup([&](int dev) -> int {
+        int optin = 0;
         KVP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
         if (smem > optin) {
             set_error("attn_bf16: needs %d B of shared memory per block, device allows %d", smem, optin);
             return KVP_ERR_UNSUPPORTED;
         }
-    }
-    {
         // setmaxnreg.inc waits until the warpgroup's registers exist in the
         // CTA's pool: refuse a build whose launch pool is smaller than the split.
         cudaFuncAttributes fa;
@@ -1139,13 +1137,11 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
                       fa.numRegs, (kRegsLow * 128 + 2 * kRegsHigh * 128 + kThreads - 1) / kThreads);
             return KVP_ERR_UNSUPPORTED;
         }
-    }
-    static int configured_smem = 0;
-    if (configured_smem != smem) {
         KVP_CUDA(cudaFuncSetAttribute(attn_bf16_sm100_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        configured_smem = smem;
-    }
+        return KVP_OK;
+    });
+    if (rc_setup != KVP_OK) return rc_setup;
     const long long grid = (long long)d.nheads * P.items_per_head;
     if (grid <= 0 || grid > 0x7fffffffLL) return KVP_ERR_ARG;
     attn_bf16_sm100_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(maps, P);

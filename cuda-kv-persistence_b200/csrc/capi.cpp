@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "kernels.h"
@@ -21,8 +22,10 @@ thread_local char g_err[512] = "";
 // One device status word per device, allocated on first use.
 int* status_word() {
     static int* words[64] = {nullptr};
+    static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> g(mu);
     if (!words[dev]) {
         int* p = nullptr;
         if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;

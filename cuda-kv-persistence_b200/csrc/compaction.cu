@@ -5,6 +5,8 @@
 // HBM-bound byte movement: every byte is read once and written once with
 // 16-byte accesses, consecutive lanes on consecutive 16-byte words.  A row
 // here is one token's K row or V row (D elements, 3 KB in bf16 at D=1536).
+#include <atomic>
+
 #include "kernels.h"
 #include "kvp_common.h"
 
@@ -64,12 +66,14 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherLayers L, int la
 }
 
 int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
+    static std::atomic<int> counts[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    int n = counts[dev].load(std::memory_order_relaxed);
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        counts[dev].store(n, std::memory_order_relaxed);
     }
     return n;
 }

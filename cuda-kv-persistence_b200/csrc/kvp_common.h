@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstddef>
+#include <mutex>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -26,6 +27,26 @@ const char* last_error();
 
 // Returns KVP_ERR_CUDA and records the message when e != cudaSuccess.
 int cuda_status(cudaError_t e, const char* what);
+
+// Per-device one-time setup (kernel attributes, launch checks): `run` is
+// called under a lock until it succeeds once on the current device; later
+// calls on that device return KVP_OK at once.  A failed setup is retried
+// (and re-reports its error) on the next call.
+struct PerDeviceOnce {
+    static constexpr int kMaxDevices = 64;
+    std::mutex mu;
+    bool done[kMaxDevices] = {};
+    template <class F>
+    int operator()(F&& run) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KVP_ERR_CUDA;
+        std::lock_guard<std::mutex> g(mu);
+        if (done[dev]) return KVP_OK;
+        const int rc = run(dev);
+        if (rc == KVP_OK) done[dev] = true;
+        return rc;
+    }
+};
 
 }  // namespace kvp
 
