@@ -142,6 +142,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
         : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
     return ok != 0;
 }
+// Non-blocking check of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+    return ok != 0;
+}
 // try_wait that lets the hardware suspend the thread until the phase
 // completes (or kSuspendNs passes), so a waiting warp takes no issue slots
 // from the softmax warps that share its SM sub-partition.
@@ -235,14 +243,16 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
-// One 128x128x128 GEMM as eight back-to-back K16 MMAs from a single asm
-// block: the descriptors of steps 1..7 are immediate offsets of step 0's, so
-// nothing but an add sits between two MMA issues and the tensor core's
-// shallow instruction queue never runs dry inside a GEMM.
+// One 128x128x128 GEMM as eight back-to-back K16 MMAs, issued in two asm
+// blocks (steps 0-5, then 6-7) so the issuer can test the next GEMM's
+// barriers while the first six are queued.  The descriptors of steps 1..7
+// are immediate offsets of step 0's: nothing but an add sits between two MMA
+// issues, and the tensor core's shallow instruction queue never runs dry
+// inside a GEMM.
 //   S = Q K^T: A and B K-major, 128B swizzle, two 64-column panels 16 KB
 //   apart: step ks starts (ks>>2)*16384 + (ks&3)*32 bytes in, i.e. adds
 //   (ks>>2)*1024 + (ks&3)*2 to the 16-byte address field.
-__device__ __forceinline__ void tc_gemm_ss(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc) {
+__device__ __forceinline__ void tc_gemm_ss_head(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc) {
     asm volatile(
         "{\n\t.reg .pred pf, pt;\n\t.reg .b64 a, b;\n\t"
         "setp.ne.b32 pf, 0, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
@@ -256,7 +266,13 @@ __device__ __forceinline__ void tc_gemm_ss(uint32_t d_tmem, uint64_t a0, uint64_
         "add.s64 a, %1, 1024;\n\tadd.s64 b, %2, 1024;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
         "add.s64 a, %1, 1026;\n\tadd.s64 b, %2, 1026;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t}"
+        ::"r"(d_tmem), "l"(a0), "l"(b0), "r"(idesc));
+}
+__device__ __forceinline__ void tc_gemm_ss_tail(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred pt;\n\t.reg .b64 a, b;\n\t"
+        "setp.eq.b32 pt, 0, 0;\n\t"
         "add.s64 a, %1, 1028;\n\tadd.s64 b, %2, 1028;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, pt;\n\t"
         "add.s64 a, %1, 1030;\n\tadd.s64 b, %2, 1030;\n\t"
@@ -265,8 +281,8 @@ __device__ __forceinline__ void tc_gemm_ss(uint32_t d_tmem, uint64_t a0, uint64_
 }
 //   O (+)= P V: P from TMEM (step ks at column +8*ks), V MN-major with step
 //   ks 16 rows = 2048 bytes further (+128 in the address field).
-__device__ __forceinline__ void tc_gemm_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
-                                           uint32_t accumulate) {
+__device__ __forceinline__ void tc_gemm_ts_head(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
+                                                uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred pf, pt;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
         "setp.ne.b32 pf, %4, 0;\n\tsetp.eq.b32 pt, 0, 0;\n\t"
@@ -280,12 +296,18 @@ __device__ __forceinline__ void tc_gemm_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         "add.s32 a, %1, 32;\n\tadd.s64 b, %2, 512;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
         "add.s32 a, %1, 40;\n\tadd.s64 b, %2, 640;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void tc_gemm_ts_tail(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred pt;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
+        "setp.eq.b32 pt, 0, 0;\n\t"
         "add.s32 a, %1, 48;\n\tadd.s64 b, %2, 768;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t"
         "add.s32 a, %1, 56;\n\tadd.s64 b, %2, 896;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, pt;\n\t}"
-        ::"r"(d_tmem), "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate));
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b0), "r"(idesc));
 }
 
 #define KVP_TMEM_LD32(taddr, r)                                                                  \
@@ -851,44 +873,75 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             uint32_t ks = 0, kph = 0;          // K ring stage / parity of tile j
             uint32_t vs = 0, vph = 0;          // V ring stage / parity of tile j
             uint32_t pvs = 0, pvph = 0;        // ... of tile j-1
+            // While the first six MMAs of a GEMM are queued, the barriers of
+            // the next GEMM are tested without blocking; a GEMM whose inputs
+            // were seen ready then follows without a wait.  (A completed phase
+            // stays completed until this thread's own later MMAs let it move.)
+            bool k_known = false;              // K(j) seen landed
             for (int j = 0; ok && j < n_tiles; ++j) {
-                if (!mbar_wait(&sm.bar_kfull[ks], kph, sm, P.status)) { ok = false; break; }
+                if (!k_known && !mbar_wait(&sm.bar_kfull[ks], kph, sm, P.status)) { ok = false; break; }
                 tc_fence_after();
+                const bool pv1 = j >= 1 && j - 1 < n1;
+                bool pv1_ready = false;
                 if (j < n0) {
-                    tc_gemm_ss(s0_tm, dq0, dk + ks * kStageDesc, idS);
+                    const uint64_t kd = dk + ks * kStageDesc;
+                    tc_gemm_ss_head(s0_tm, dq0, kd, idS);
+                    if (pv1)
+                        pv1_ready = (j - 1 < n0 || mbar_test(&sm.bar_vfull[pvs], pvph)) &&
+                                    mbar_test(&sm.bar_p_full[1], (uint32_t)(j - 1) & 1u);
+                    tc_gemm_ss_tail(s0_tm, dq0, kd, idS);
                     tc_commit(&sm.bar_s_full[0]);
                 }
-                if (j >= 1 && j - 1 < n1) {    // PV1(j-1)
-                    if (j - 1 >= n0 && !mbar_wait(&sm.bar_vfull[pvs], pvph, sm, P.status)) { ok = false; break; }
-                    if (!mbar_wait(&sm.bar_p_full[1], (uint32_t)(j - 1) & 1u, sm, P.status)) { ok = false; break; }
+                if (pv1) {                     // PV1(j-1)
+                    if (!pv1_ready) {
+                        if (j - 1 >= n0 && !mbar_wait(&sm.bar_vfull[pvs], pvph, sm, P.status)) { ok = false; break; }
+                        if (!mbar_wait(&sm.bar_p_full[1], (uint32_t)(j - 1) & 1u, sm, P.status)) { ok = false; break; }
+                    }
                     tc_fence_after();
-                    tc_gemm_ts(o1_tm, s1_tm, dv + pvs * kStageDesc, idO, j > 1 ? 1u : 0u);
+                    const uint64_t vd = dv + pvs * kStageDesc;
+                    tc_gemm_ts_head(o1_tm, s1_tm, vd, idO, j > 1 ? 1u : 0u);
+                    tc_gemm_ts_tail(o1_tm, s1_tm, vd, idO);
                     if (j == n1) tc_commit(&sm.bar_o_done[1]);
                     if (own_release) tc_commit(&sm.bar_vempty[pvs]);
                 }
+                bool pv0_ready = false;
                 if (j < n1) {
-                    tc_gemm_ss(s1_tm, dq1, dk + ks * kStageDesc, idS);
+                    const uint64_t kd = dk + ks * kStageDesc;
+                    tc_gemm_ss_head(s1_tm, dq1, kd, idS);
+                    if (j < n0)
+                        pv0_ready = mbar_test(&sm.bar_vfull[vs], vph) &&
+                                    mbar_test(&sm.bar_p_full[0], (uint32_t)j & 1u);
+                    tc_gemm_ss_tail(s1_tm, dq1, kd, idS);
                     tc_commit(&sm.bar_s_full[1]);
                 }
                 if (own_release) tc_commit(&sm.bar_kempty[ks]);
+                const uint32_t ks_n = ks + 1 == kKStages ? 0u : ks + 1;
+                const uint32_t kph_n = ks + 1 == kKStages ? kph ^ 1u : kph;
+                k_known = false;
                 if (j < n0) {                  // PV0(j)
-                    if (!mbar_wait(&sm.bar_vfull[vs], vph, sm, P.status)) { ok = false; break; }
-                    if (!mbar_wait(&sm.bar_p_full[0], (uint32_t)j & 1u, sm, P.status)) { ok = false; break; }
+                    if (!pv0_ready) {
+                        if (!mbar_wait(&sm.bar_vfull[vs], vph, sm, P.status)) { ok = false; break; }
+                        if (!mbar_wait(&sm.bar_p_full[0], (uint32_t)j & 1u, sm, P.status)) { ok = false; break; }
+                    }
                     tc_fence_after();
-                    tc_gemm_ts(o0_tm, s0_tm, dv + vs * kStageDesc, idO, j > 0 ? 1u : 0u);
+                    const uint64_t vd = dv + vs * kStageDesc;
+                    tc_gemm_ts_head(o0_tm, s0_tm, vd, idO, j > 0 ? 1u : 0u);
+                    if (j + 1 < n_tiles) k_known = mbar_test(&sm.bar_kfull[ks_n], kph_n);
+                    tc_gemm_ts_tail(o0_tm, s0_tm, vd, idO);
                     if (j == n0 - 1) tc_commit(&sm.bar_o_done[0]);
                     if (own_release && j >= n1) tc_commit(&sm.bar_vempty[vs]);   // no PV1 reads V(j)
                 }
                 pvs = vs; pvph = vph;
                 if (++vs == kVStages) { vs = 0; vph ^= 1u; }
-                if (++ks == kKStages) { ks = 0; kph ^= 1u; }
+                ks = ks_n; kph = kph_n;
             }
             if (ok && n_tiles > 0 && n_tiles - 1 < n1) {   // PV1(last)
                 const int jl = n_tiles - 1;
                 if ((jl < n0 || mbar_wait(&sm.bar_vfull[pvs], pvph, sm, P.status)) &&
                     mbar_wait(&sm.bar_p_full[1], (uint32_t)jl & 1u, sm, P.status)) {
                     tc_fence_after();
-                    tc_gemm_ts(o1_tm, s1_tm, dv + pvs * kStageDesc, idO, jl > 0 ? 1u : 0u);
+                    tc_gemm_ts_head(o1_tm, s1_tm, dv + pvs * kStageDesc, idO, jl > 0 ? 1u : 0u);
+                    tc_gemm_ts_tail(o1_tm, s1_tm, dv + pvs * kStageDesc, idO);
                     tc_commit(&sm.bar_o_done[1]);
                     if (own_release) tc_commit(&sm.bar_vempty[pvs]);
                 }
