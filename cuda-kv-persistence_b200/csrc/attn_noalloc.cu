@@ -97,7 +97,7 @@ KVP_API int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d
                    io->q_rows, io->kv_rows, io->arena_rows};
     kvp::AttnDesc A{d->tokens, d->frames, d->q_frame0, d->mode, d->window,
                     d->heads, d->head_dim, d->head0, d->nheads, d->flat};
-    rc = kvp::launch_attn_bf16(L, A, status, s);
+    rc = kvp::launch_attn_bf16(L, A, status, s, /*allow_split=*/false);
     if (rc != kvp::KVP_OK) return rc;
     if (host_status) {
         KVP_CUDA(cudaMemcpyAsync(host_status, status, sizeof(int), cudaMemcpyDeviceToHost, s));

@@ -44,6 +44,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -108,6 +109,11 @@ struct Params {
     int D, T, frames, q_frame0, mode, window, head0, nheads, flat, items_per_head, n_qt, n_pairs;
     int base_boxes, arena_boxes;   // box kinds usable (heights <= tensor rows); 0 = no arena TMA
     float scale_log2;
+    // Key-range split (per-frame tiling only): splits > 1 writes fp32 partial
+    // (O, m, l) to ws instead of bf16 output; combine_splits_kernel merges.
+    int splits;
+    float* ws;
+    long long ws_rows;             // query rows of the launch (frames * T)
 };
 
 // ------------------------------------------------------------- primitives
@@ -458,6 +464,7 @@ struct Work {
     long long klo;       // first key row, shared by both query tiles
     long long khi;       // end of the staged key rows (max over the tiles)
     int n_tiles;         // K/V tiles staged (max over the tiles)
+    int chunk;           // key-range chunk of this CTA (0 without a split)
     QTile t[kQTiles];
 };
 
@@ -466,6 +473,7 @@ __device__ __forceinline__ Work decode_work(const Params& P) {
     const int h_local = blockIdx.x / P.items_per_head;
     const int i = blockIdx.x % P.items_per_head;
     w.head = P.head0 + h_local;
+    w.chunk = 0;
     const long long T = P.T;
     if (P.flat) {
         const long long R0 = (long long)P.q_frame0 * T;
@@ -488,7 +496,10 @@ __device__ __forceinline__ Work decode_work(const Params& P) {
             x.khi_lo = (ff + 1) * T;
         }
     } else {
-        const int fr = i / P.n_pairs, pr = i % P.n_pairs;
+        // item = (frame, query tile pair, key chunk), chunk fastest
+        w.chunk = i % P.splits;
+        const int ip = i / P.splits;
+        const int fr = ip / P.n_pairs, pr = ip % P.n_pairs;
         const int f = P.q_frame0 + P.frames - 1 - fr;  // longest key span first
         if (P.mode == 0) {
             w.klo = (long long)f * T;
@@ -519,6 +530,24 @@ __device__ __forceinline__ Work decode_work(const Params& P) {
             x.n_tiles = 0;
         }
         if (x.n_tiles > w.n_tiles) w.n_tiles = x.n_tiles;
+    }
+    if (!P.flat && P.splits > 1) {
+        // Both tiles of a per-frame pair share one key span: chunk c takes
+        // whole 128-key tiles [c*per, (c+1)*per).  Rows keep their own key
+        // limit (x.khi) for masking; the staged range ends at the chunk.
+        const int total = w.n_tiles;
+        const int per = (total + P.splits - 1) / P.splits;
+        const int t0 = w.chunk * per;
+        const int t1 = t0 + per < total ? t0 + per : total;
+        const int nt = t1 > t0 ? t1 - t0 : 0;
+        const long long klo0 = w.klo;
+        w.klo = klo0 + (long long)t0 * kBN;
+        const long long kend = klo0 + (long long)t1 * kBN;
+        w.khi = nt > 0 ? (kend < w.khi ? kend : w.khi) : w.klo;
+        w.n_tiles = nt;
+#pragma unroll
+        for (int q = 0; q < kQTiles; ++q)
+            if (w.t[q].nq > 0) w.t[q].n_tiles = nt;
     }
     return w;
 }
@@ -1023,7 +1052,41 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             tc_fence_before();
             mbar_arrive(&sm.bar_p_full[qt]);
         }
-        if (ok && t.n_tiles > 0 && warp_wait(&sm.bar_o_done[qt], 0, sm, P.status)) {
+        if (P.splits > 1) {
+            // partial (O, m, l) of this key chunk, fp32, for combine_splits_kernel
+            const long long rr = t.row0 + row - (long long)P.q_frame0 * P.T;
+            const size_t slot = ((size_t)w.chunk * (size_t)P.ws_rows + (size_t)rr) * (size_t)P.nheads +
+                                (size_t)(w.head - P.head0);
+            float* wo = P.ws + slot * kDH;
+            float* wml = P.ws + (size_t)P.splits * (size_t)P.ws_rows * (size_t)P.nheads * kDH + slot * 2;
+            if (t.nq > 0 && t.n_tiles > 0) {
+                if (ok && warp_wait(&sm.bar_o_done[qt], 0, sm, P.status)) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        uint32_t o[32];
+                        KVP_TMEM_LD32(o_tm + 32 * c4, o);
+                        tmem_wait_ld();
+                        if (row < t.nq) {
+#pragma unroll
+                            for (int c = 0; c < 32; c += 4)
+                                *reinterpret_cast<uint4*>(wo + 32 * c4 + c) =
+                                    make_uint4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+                        }
+                    }
+                    if (row < t.nq) {
+                        wml[0] = m_run;
+                        wml[1] = l_run;
+                    }
+                }
+            } else if (t.nq > 0 && row < t.nq) {   // empty chunk: identity partial
+#pragma unroll
+                for (int c = 0; c < kDH; c += 4)
+                    *reinterpret_cast<uint4*>(wo + c) = make_uint4(0, 0, 0, 0);
+                wml[0] = -INFINITY;
+                wml[1] = 0.f;
+            }
+        } else if (ok && t.n_tiles > 0 && warp_wait(&sm.bar_o_done[qt], 0, sm, P.status)) {
             tc_fence_after();
             const float inv = 1.f / l_run;
             __nv_bfloat16* dst = P.out + (size_t)(t.row0 + row) * D + hcol;
@@ -1052,6 +1115,90 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
+}
+
+// ---------------------------------------------------------- split combine
+// out[row, head] = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c over the
+// key chunks c of a split launch (M = max_c m_c; m in log2 units).  One warp
+// per (query row, head), four dims per lane.
+__global__ void __launch_bounds__(256)
+combine_splits_kernel(const float* __restrict__ ws, __nv_bfloat16* __restrict__ out, int splits,
+                      long long rows, int nheads, int D, int head0, long long row0) {
+    const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (gw >= rows * nheads) return;
+    const long long rr = gw / nheads;
+    const int h = (int)(gw % nheads);
+    const float* ml = ws + (size_t)splits * (size_t)rows * (size_t)nheads * kDH;
+    float M = -INFINITY;
+    for (int c = 0; c < splits; ++c)
+        M = fmaxf(M, ml[(((size_t)c * rows + rr) * nheads + h) * 2]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = 0; c < splits; ++c) {
+        const size_t slot = ((size_t)c * rows + rr) * nheads + h;
+        const float m = ml[slot * 2];
+        if (m == -INFINITY) continue;                 // chunk without keys for this row
+        const float wgt = exp2f(m - M);
+        L += wgt * ml[slot * 2 + 1];
+        const float4 o = reinterpret_cast<const float4*>(ws + slot * kDH)[lane];
+        acc.x += wgt * o.x; acc.y += wgt * o.y; acc.z += wgt * o.z; acc.w += wgt * o.w;
+    }
+    const float inv = 1.f / L;
+    uint2 pk;
+    pk.x = pack_bf16(acc.x * inv, acc.y * inv);
+    pk.y = pack_bf16(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(out + (size_t)(row0 + rr) * D + (size_t)(head0 + h) * kDH + 4 * lane) = pk;
+}
+
+// The split workspace comes from a private, per-device stream-ordered pool
+// that keeps freed blocks cached (release threshold = max): the default
+// pool would hand its memory back to the driver at every synchronisation
+// and each launch would map it again.
+cudaError_t workspace_pool(cudaMemPool_t* out) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    if (!pools[dev]) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t p = nullptr;
+        e = cudaMemPoolCreate(&p, &props);
+        if (e != cudaSuccess) return e;
+        uint64_t keep = ~0ull;
+        e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) {
+            cudaMemPoolDestroy(p);
+            return e;
+        }
+        pools[dev] = p;
+    }
+    *out = pools[dev];
+    return cudaSuccess;
+}
+
+// Key chunks per (query tile pair, head) for a per-frame launch: split only
+// when the launch has fewer CTAs than SMs; minimise waves x (fixed cost +
+// tiles per chunk), the fixed cost (prologue, epilogue) ~ 3 tiles.
+int choose_splits(long long items, int tiles_max, int sms) {
+    if (items <= 0 || items >= sms || tiles_max < 4) return 1;
+    int best = 1;
+    long long best_cost = -1;
+    for (int c = 1; c <= 8 && c <= tiles_max / 2; ++c) {
+        const long long waves = (items * c + sms - 1) / sms;
+        const long long cost = waves * (3 + (tiles_max + c - 1) / c);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = c;
+        }
+    }
+    return best;
 }
 
 // ------------------------------------------------------------ host helpers
@@ -1098,7 +1245,8 @@ int make_map(CUtensorMap* m, const void* base, long long rows, long long cols, l
 
 }  // namespace
 
-int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream) {
+int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
+                     bool allow_split) {
     const long long T = d.tokens;
     const int D = d.heads * kDH;
     if (d.head_dim != kDH || d.heads <= 0 || T <= 0 || d.frames <= 0 || d.q_frame0 < 0 ||
@@ -1171,6 +1319,9 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
     P.base_boxes = base_boxes;
     P.arena_boxes = arena_boxes;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)kDH);
+    P.splits = 1;
+    P.ws = nullptr;
+    P.ws_rows = (long long)d.frames * T;
 
     const int smem = (int)sizeof(Smem);
     static PerDeviceOnce setup;
@@ -1195,10 +1346,49 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
         return KVP_OK;
     });
     if (rc_setup != KVP_OK) return rc_setup;
+    // Key-range split for per-frame launches that would leave SMs idle
+    // (KVP_ATTN_SPLITS=n forces n, 1 disables).
+    if (!d.flat && allow_split) {
+        int sms = 148, dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess)
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int last = d.q_frame0 + d.frames - 1;
+        const long long span = d.mode == 0 ? T
+            : (long long)((d.window > 0 && d.window < last + 1) ? d.window : last + 1) * T;
+        const int tiles_max = (int)((span + kBN - 1) / kBN);
+        int splits = choose_splits((long long)d.nheads * P.items_per_head, tiles_max, sms);
+        if (const char* e = std::getenv("KVP_ATTN_SPLITS")) {
+            const int f = std::atoi(e);
+            if (f >= 1) splits = f < tiles_max ? f : (tiles_max > 0 ? tiles_max : 1);
+        }
+        P.splits = splits > 1 ? splits : 1;
+    }
+    if (P.splits > 1) {
+        P.items_per_head *= P.splits;
+        const size_t ws_bytes = (size_t)P.splits * (size_t)P.ws_rows * (size_t)d.nheads * (kDH + 2) *
+                                sizeof(float);
+        cudaMemPool_t pool = nullptr;
+        KVP_CUDA(workspace_pool(&pool));
+        KVP_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&P.ws), ws_bytes, pool, stream));
+    }
     const long long grid = (long long)d.nheads * P.items_per_head;
-    if (grid <= 0 || grid > 0x7fffffffLL) return KVP_ERR_ARG;
+    if (grid <= 0 || grid > 0x7fffffffLL) {
+        if (P.ws) cudaFreeAsync(P.ws, stream);
+        return KVP_ERR_ARG;
+    }
     attn_bf16_sm100_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(maps, P);
-    KVP_CUDA(cudaGetLastError());
+    cudaError_t le = cudaGetLastError();
+    if (P.splits > 1) {
+        if (le == cudaSuccess) {
+            const long long warps = P.ws_rows * d.nheads;
+            combine_splits_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(
+                P.ws, P.out, P.splits, P.ws_rows, d.nheads, D, d.head0, (long long)d.q_frame0 * T);
+            le = cudaGetLastError();
+        }
+        const cudaError_t fe = cudaFreeAsync(P.ws, stream);
+        if (le == cudaSuccess) le = fe;
+    }
+    if (le != cudaSuccess) return cuda_status(le, "attn_bf16 launch");
     return KVP_OK;
 }
 

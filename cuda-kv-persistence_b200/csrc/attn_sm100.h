@@ -45,7 +45,13 @@ struct AttnDesc {
     int flat;
 };
 
-int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream);
+// Per-frame (non-flat) launches whose CTAs would not fill the SMs split each
+// query tile pair's key range over several CTAs and merge their partial
+// (O, max, sum) with a second kernel; the fp32 workspace is stream-ordered
+// (a private memory pool that keeps its blocks cached).  allow_split = false
+// (callers that may not allocate) always runs one CTA per pair.
+int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
+                     bool allow_split = true);
 
 // A kernel whose bounded mbarrier wait cannot complete: records
 // KVP_STATUS_TIMEOUT after limit_ns (<= 5 s).  For tests of the timeout path.

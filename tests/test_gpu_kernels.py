@@ -236,3 +236,20 @@ def test_bf16_head_subset_and_frame_offset(cuda):
     sl = slice(2 * T, 3 * T)
     check_bf16(got[sl, 128:], want[sl, 128:], "subset")
     assert np.all(got[sl, :128] == 0) and np.all(got[: 2 * T] == 0)
+
+
+@pytest.mark.parametrize("splits", ["1", "3", "7"])
+def test_bf16_key_split_matches_oracle(cuda, monkeypatch, splits):
+    """Per-frame launches with the key range split over several CTAs (forced
+    through KVP_ATTN_SPLITS; 7 leaves some chunks of the short frames empty):
+    same results as the oracle, and policies stay bitwise identical."""
+    monkeypatch.setenv("KVP_ATTN_SPLITS", splits)
+    F, T, H = 4, 300, 2
+    D, q, k, v = _bf16_case(F, T, H, seed=21)
+    want = attention_frames(q, k, v, frames=F, tokens=T, heads=H, head_dim=128, mode="cross")
+    m = _scattered_map(F * T, 200, seed=22)
+    arena = build_arena(k, v, m, 200)
+    a = _run_bf16(q, k, v, m, arena, tokens=T, frames=F, heads=H, mode="causal")
+    b = _run_bf16(q, k, v, None, None, tokens=T, frames=F, heads=H, mode="causal")
+    assert np.array_equal(a, b)
+    check_bf16(a, want, ("split", splits))
