@@ -1220,9 +1220,56 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// Encoded maps are cached by (base, rows, cols, pitch, box): a map holds no
+// more than these, so an entry stays right even if the memory is freed and
+// reused with the same shape.  Per-frame loops launch the same few tensors
+// hundreds of times.
+struct MapKey {
+    const void* base;
+    long long rows, cols, pitch;
+    uint32_t box;
+    bool operator==(const MapKey& o) const {
+        return base == o.base && rows == o.rows && cols == o.cols && pitch == o.pitch && box == o.box;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        size_t h = std::hash<const void*>()(k.base);
+        h ^= std::hash<long long>()(k.rows) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+        h ^= std::hash<long long>()(k.cols * 131 + k.pitch) + (h << 6) + (h >> 2);
+        h ^= std::hash<uint32_t>()(k.box) + (h << 6) + (h >> 2);
+        return h;
+    }
+};
+
+int encode_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long pitch,
+               uint32_t box_rows);
+
 // 2D bf16 row-major tensor [rows][cols] with row pitch `pitch` elements.
 int make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long pitch,
              uint32_t box_rows) {
+    static std::mutex mu;
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{base, rows, cols, pitch, box_rows};
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *m = it->second;
+            return KVP_OK;
+        }
+    }
+    const int rc = encode_map(m, base, rows, cols, pitch, box_rows);
+    if (rc == KVP_OK) {
+        std::lock_guard<std::mutex> g(mu);
+        if (cache.size() >= 4096) cache.clear();
+        cache.emplace(key, *m);
+    }
+    return rc;
+}
+
+int encode_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long pitch,
+               uint32_t box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         set_error("cuTensorMapEncodeTiled unavailable");

@@ -49,9 +49,11 @@ Session::Session(const SessionConfig& c)
         if (e == cudaSuccess) e = cudaMalloc(&d_pairs_, pair_bytes);
         if (e == cudaSuccess && arena_layer_bytes_ > 0)
             e = cudaMalloc(&d_arena_, (size_t)arena_layer_bytes_ * c.layers);
-        if (e == cudaSuccess) e = cudaMallocHost(&h_map_pinned_, map_bytes);
-        if (e == cudaSuccess) e = cudaMallocHost(&h_pairs_pinned_, pair_bytes);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&upload_done_, cudaEventDisableTiming);
+        for (int i = 0; i < kUploadSlots && e == cudaSuccess; ++i) {
+            e = cudaMallocHost(&h_map_pinned_[i], map_bytes);
+            if (e == cudaSuccess) e = cudaMallocHost(&h_pairs_pinned_[i], pair_bytes);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&upload_done_[i], cudaEventDisableTiming);
+        }
         if (e == cudaSuccess) e = cudaMemset(d_map_, 0xff, map_bytes);  // all -1
         if (e == cudaSuccess && d_arena_)
             e = cudaMemset(d_arena_, 0, (size_t)arena_layer_bytes_ * c.layers);
@@ -60,12 +62,15 @@ Session::Session(const SessionConfig& c)
 }
 
 Session::~Session() {
-    if (upload_done_) { cudaEventSynchronize(upload_done_); cudaEventDestroy(upload_done_); }
+    for (int i = 0; i < kUploadSlots; ++i)
+        if (upload_done_[i]) { cudaEventSynchronize(upload_done_[i]); cudaEventDestroy(upload_done_[i]); }
     if (d_map_) cudaFree(d_map_);
     if (d_pairs_) cudaFree(d_pairs_);
     if (d_arena_) cudaFree(d_arena_);
-    if (h_map_pinned_) cudaFreeHost(h_map_pinned_);
-    if (h_pairs_pinned_) cudaFreeHost(h_pairs_pinned_);
+    for (int i = 0; i < kUploadSlots; ++i) {
+        if (h_map_pinned_[i]) cudaFreeHost(h_map_pinned_[i]);
+        if (h_pairs_pinned_[i]) cudaFreeHost(h_pairs_pinned_[i]);
+    }
 }
 
 void* Session::arena(int layer) const {
@@ -255,17 +260,20 @@ int Session::upload(cudaStream_t s) {
     if (!d_map_) return KVP_ERR_ARG;
     const int64_t r0 = info_.map_row0, n = info_.map_rows;
     if (r0 < 0 || n < 0 || r0 + n > (int64_t)map_.size()) return KVP_ERR_ARG;
-    // The pinned staging buffers may still feed the previous upload.
-    KVP_CUDA(cudaEventSynchronize(upload_done_));
-    std::memcpy(h_map_pinned_ + r0, map_.data() + r0, (size_t)n * sizeof(int64_t));
-    KVP_CUDA(cudaMemcpyAsync(d_map_ + r0, h_map_pinned_ + r0, (size_t)n * sizeof(int64_t),
+    // This slot's pinned buffers may still feed the upload made
+    // kUploadSlots uploads ago.
+    const int k = upload_slot_;
+    upload_slot_ = (upload_slot_ + 1) % kUploadSlots;
+    KVP_CUDA(cudaEventSynchronize(upload_done_[k]));
+    std::memcpy(h_map_pinned_[k] + r0, map_.data() + r0, (size_t)n * sizeof(int64_t));
+    KVP_CUDA(cudaMemcpyAsync(d_map_ + r0, h_map_pinned_[k] + r0, (size_t)n * sizeof(int64_t),
                              cudaMemcpyHostToDevice, s));
     if (!pairs_.empty()) {
-        std::memcpy(h_pairs_pinned_, pairs_.data(), pairs_.size() * sizeof(int32_t));
-        KVP_CUDA(cudaMemcpyAsync(d_pairs_, h_pairs_pinned_, pairs_.size() * sizeof(int32_t),
+        std::memcpy(h_pairs_pinned_[k], pairs_.data(), pairs_.size() * sizeof(int32_t));
+        KVP_CUDA(cudaMemcpyAsync(d_pairs_, h_pairs_pinned_[k], pairs_.size() * sizeof(int32_t),
                                  cudaMemcpyHostToDevice, s));
     }
-    KVP_CUDA(cudaEventRecord(upload_done_, s));
+    KVP_CUDA(cudaEventRecord(upload_done_[k], s));
     return KVP_OK;
 }
 

@@ -115,9 +115,14 @@ private:
     int32_t* d_pairs_ = nullptr;
     void* d_arena_ = nullptr;
     int64_t arena_layer_bytes_ = 0;
-    int64_t* h_map_pinned_ = nullptr;
-    int32_t* h_pairs_pinned_ = nullptr;
-    cudaEvent_t upload_done_ = nullptr;
+    // Pinned staging for the uploads, a ring of kUploadSlots: an upload only
+    // waits for the copy made kUploadSlots uploads earlier, so the host can
+    // plan the next frame while the device still works on this one.
+    static constexpr int kUploadSlots = 2;
+    int64_t* h_map_pinned_[kUploadSlots] = {};
+    int32_t* h_pairs_pinned_[kUploadSlots] = {};
+    cudaEvent_t upload_done_[kUploadSlots] = {};
+    int upload_slot_ = 0;
 };
 
 // Reference motion CSV reader (src/run_policy_experiment.cu:45-69): rows
