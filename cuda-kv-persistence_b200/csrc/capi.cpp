@@ -316,6 +316,7 @@ struct kvp_session_config {
 struct kvp_step_info {
     int frame, sel_count, staged_tiles, copies;
     long long map_row0, map_rows, window_bytes, staged_bytes;
+    int restaged, hits;
 };
 
 KVP_API void* kvp_session_create(const kvp_session_config* c) {
@@ -334,6 +335,11 @@ KVP_API void kvp_session_destroy(void* s) { delete static_cast<kvp::Session*>(s)
 KVP_API int kvp_session_plan_frame(void* s, int frame, const float* scores_flat) {
     return static_cast<kvp::Session*>(s)->plan_frame(frame, scores_flat);
 }
+KVP_API int kvp_session_plan_frame_reuse(void* s, int frame, const float* scores_flat,
+                                         const signed char* reuse_flat) {
+    return static_cast<kvp::Session*>(s)->plan_frame(frame, scores_flat,
+                                                     reinterpret_cast<const int8_t*>(reuse_flat));
+}
 KVP_API int kvp_session_plan_stack(void* s, const float* scores_flat) {
     return static_cast<kvp::Session*>(s)->plan_stack(scores_flat);
 }
@@ -349,6 +355,8 @@ KVP_API int kvp_session_info(void* s, kvp_step_info* out) {
     out->map_rows = i.map_rows;
     out->window_bytes = i.window_bytes;
     out->staged_bytes = i.staged_bytes;
+    out->restaged = i.restaged;
+    out->hits = i.hits;
     return kvp::KVP_OK;
 }
 KVP_API long long kvp_session_slots(void* s) { return static_cast<kvp::Session*>(s)->slots(); }
@@ -391,6 +399,14 @@ KVP_API int kvp_session_stage_layer(void* s, int layer, const void* k, const voi
 }
 KVP_API int kvp_session_window(void* s, int layer, void* stream) {
     return static_cast<kvp::Session*>(s)->apply_window(layer, (cudaStream_t)stream);
+}
+KVP_API int kvp_session_step(void* s, int frame, const float* scores_flat,
+                             const signed char* reuse_flat, const void* const* k_layers,
+                             const void* const* v_layers, int window_layer, void* stream) {
+    return static_cast<kvp::Session*>(s)->step(frame, scores_flat,
+                                                reinterpret_cast<const int8_t*>(reuse_flat),
+                                                k_layers, v_layers, window_layer,
+                                                (cudaStream_t)stream);
 }
 KVP_API int kvp_session_clear_window(void* s, void* stream) {
     return static_cast<kvp::Session*>(s)->clear_window((cudaStream_t)stream);

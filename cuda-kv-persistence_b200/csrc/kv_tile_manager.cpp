@@ -216,9 +216,10 @@ bool KVTileManager::streaming_begin() {
 }
 
 bool KVTileManager::streaming_reserve(long row_id, size_t bytes_kv, bool changed, long* out_slot,
-                                      bool* copy_needed) {
+                                      bool* copy_needed, bool* was_held) {
     // :153-192 -- a sticky hit costs nothing unless the row changed.
     auto it = row_slot_.find(row_id);
+    if (was_held) *was_held = it != row_slot_.end();
     if (it != row_slot_.end()) {
         *out_slot = it->second;
         if (!changed) { *copy_needed = false; return true; }

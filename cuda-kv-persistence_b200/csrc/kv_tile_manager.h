@@ -83,8 +83,9 @@ public:
     // session's multi-layer gather kernel).  Same results as the staging
     // calls above; *copy_needed tells whether the row's data must be written.
     bool arena_reserve(size_t row_bytes_kv, long* out_row);
+    // *was_held (optional) tells whether row_id held a slot before the call.
     bool streaming_reserve(long row_id, size_t row_bytes_kv, bool changed, long* out_slot,
-                           bool* copy_needed);
+                           bool* copy_needed, bool* was_held = nullptr);
     // Span in bytes the next window would cover, 0 when none would be applied.
     size_t arena_window_span() const;
     size_t streaming_window_span() const;

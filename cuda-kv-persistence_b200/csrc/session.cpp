@@ -13,7 +13,8 @@ Session::Session(const SessionConfig& c)
     : c_(c), layout_(c.tokens > 0 ? c.tokens : 1, c.tile_tokens > 0 ? c.tile_tokens : 1) {
     if (c.frames <= 0 || c.tokens <= 0 || c.hidden <= 0 || c.tile_tokens <= 0 ||
         (c.elem_bytes != 2 && c.elem_bytes != 4) || c.set_aside < 0 || c.layers < 0 ||
-        c.layers > kMaxLayers || c.mode < MODE_INTRA || c.mode > MODE_STACK || c.window < 0 ||
+        c.layers > kMaxLayers || c.mode < MODE_INTRA || c.mode > MODE_REUSE || c.window < 0 ||
+        (c.mode == MODE_REUSE && !c.streaming) ||
         (2 * (int64_t)c.hidden * c.elem_bytes) % 16 != 0) {
         set_error("session: invalid configuration");
         status_ = KVP_ERR_ARG;
@@ -100,15 +101,20 @@ int Session::stage_rows_of(int64_t gid, int64_t src_f, int64_t tile) {
             if (copy) {
                 pairs_.push_back((int32_t)row_id);
                 pairs_.push_back((int32_t)slot);
+            } else if (c_.streaming) {
+                ++info_.hits;
             }
         }
     }
     return all ? 1 : 0;
 }
 
-int Session::plan_frame(int f, const float* scores_flat) {
+int Session::plan_frame(int f, const float* scores_flat, const int8_t* reuse_flat) {
     if (status_ != KVP_OK) return status_;
-    if (c_.mode == MODE_STACK || f < 0 || f >= c_.frames || !scores_flat || f != last_frame_ + 1 ||
+    if (c_.mode == MODE_REUSE && f >= 0 && f < c_.frames && scores_flat && f == last_frame_ + 1 &&
+        !finished_)
+        return plan_reuse(f, scores_flat, reuse_flat);
+    if (c_.mode == MODE_STACK || c_.mode == MODE_REUSE || f < 0 || f >= c_.frames || !scores_flat || f != last_frame_ + 1 ||
         finished_) {
         set_error("plan_frame: frame %d out of order (expected %d) or wrong mode", f, last_frame_ + 1);
         return KVP_ERR_ARG;
@@ -179,6 +185,72 @@ int Session::plan_frame(int f, const float* scores_flat) {
         } else {
             mgr_->arena_end_step();
         }
+    }
+    last_frame_ = f;
+    return KVP_OK;
+}
+
+int Session::plan_reuse(int f, const float* scores_flat, const int8_t* reuse_flat) {
+    // The intra streaming loop of src/run_policy_experiment.cu:156-274 with
+    // position keys and changed = !reuse[f][tile] in streaming_stage
+    // (src/kv_tile_manager.cu:153-175).
+    int count = 0;
+    info_ = SessionStepInfo{};
+    info_.frame = f;
+    pairs_.clear();
+    sel_ids_.clear();
+    const bool persist = c_.policy != POLICY_NONE;
+    if (persist) {
+        policy_->select(scores_flat + (int64_t)f * nt_, (int)nt_, (int)slots_, ids_.data(), &count);
+        sel_ids_.assign(ids_.begin(), ids_.begin() + std::max(0, count));
+    }
+    info_.sel_count = count;
+    std::fill(selected_.begin(), selected_.begin() + nt_, 0);
+    for (int i = 0; i < count; ++i)
+        if (ids_[i] >= 0 && ids_[i] < nt_) selected_[(size_t)ids_[i]] = 1;
+    if (persist && f > 0) {
+        for (int64_t tile = 0; tile < nt_; ++tile) {
+            if (!prev_selected_[(size_t)tile] || selected_[(size_t)tile]) continue;
+            const int64_t t0 = layout_.tile_start(tile);
+            const int64_t cnt = layout_.tile_count(tile);
+            // Last row first: the LIFO free stack then hands these slots to
+            // the next admitted tile in ascending order, so its 8-row groups
+            // stay single ascending runs the kernel stages with TMA boxes.
+            for (int64_t r = cnt - 1; r >= 0; --r) mgr_->streaming_release((long)(t0 + r));
+        }
+    }
+    int64_t* map = map_.data() + (int64_t)f * c_.tokens;
+    std::fill(map, map + c_.tokens, -1);
+    int tiles_ok = 0;
+    for (int i = 0; persist && i < count; ++i) {
+        if (ids_[i] < 0 || ids_[i] >= nt_) continue;
+        const int64_t tile = ids_[i];
+        const int64_t t0 = layout_.tile_start(tile);
+        const int64_t cnt = layout_.tile_count(tile);
+        const bool changed = !(reuse_flat && reuse_flat[(int64_t)f * nt_ + tile]);
+        bool all = true;
+        for (int64_t r = 0; r < cnt && all; ++r) {
+            long slot = -1;
+            bool copy = false, held = false;
+            all = mgr_->streaming_reserve((long)(t0 + r), (size_t)(2 * row_kv_bytes_), changed, &slot,
+                                          &copy, &held);
+            if (!all) break;
+            map[t0 + r] = slot;
+            if (!copy) { ++info_.hits; continue; }
+            if (held) ++info_.restaged;
+            pairs_.push_back((int32_t)((int64_t)f * c_.tokens + t0 + r));
+            pairs_.push_back((int32_t)slot);
+        }
+        if (all) ++tiles_ok;
+    }
+    info_.staged_tiles = tiles_ok;
+    info_.copies = (int)(pairs_.size() / 2);
+    info_.map_row0 = (int64_t)f * c_.tokens;
+    info_.map_rows = c_.tokens;
+    if (persist) {
+        info_.window_bytes = (int64_t)mgr_->streaming_window_span();
+        info_.staged_bytes = (int64_t)mgr_->streaming_staged_bytes();
+        std::copy(selected_.begin(), selected_.begin() + nt_, prev_selected_.begin());
     }
     last_frame_ = f;
     return KVP_OK;
@@ -323,6 +395,16 @@ int Session::clear_window(cudaStream_t s) {
     attr.accessPolicyWindow.missProp = cudaAccessPropertyNormal;
     KVP_CUDA(cudaStreamSetAttribute(s, cudaStreamAttributeAccessPolicyWindow, &attr));
     return KVP_OK;
+}
+
+int Session::step(int f, const float* scores_flat, const int8_t* reuse_flat,
+                  const void* const* k_layers, const void* const* v_layers, int window_layer,
+                  cudaStream_t s) {
+    int rc = plan_frame(f, scores_flat, reuse_flat);
+    if (rc != KVP_OK || c_.policy == POLICY_NONE) return rc;
+    if ((rc = upload(s)) != KVP_OK) return rc;
+    if ((rc = stage(k_layers, v_layers, s)) != KVP_OK) return rc;
+    return window_layer >= 0 ? apply_window(window_layer, s) : KVP_OK;
 }
 
 int read_motion_csv(const char* path, int frames, int num_tiles, float* scores, int8_t* reuse) {

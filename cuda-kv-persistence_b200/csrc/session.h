@@ -13,6 +13,13 @@
 //     first frame (total_frames - base); ids are offset to absolute gids;
 //   * stack: one admission over all frames' tiles (the cross step of the last
 //     frame), one KVMap shared by every query frame of a causal stack.
+//   * reuse (temporal reuse, streaming only): intra attention, but a row's
+//     streaming slot is keyed by its token position t0+r, so a tile keeps
+//     its slots from frame to frame while the policy keeps selecting it; a
+//     tile flagged unchanged (the motion CSV's reuse column) is a sticky hit
+//     and copies nothing, a changed tile is re-copied into the slots it
+//     holds.  The reference loads that column (src/run_policy_experiment.cu:
+//     114-118) but stages with changed = false (:211).
 // The device side keeps one arena per layer (all layers share the admission:
 // motion scores are per tile, not per layer) and stages every layer's rows
 // with one gather launch.
@@ -31,7 +38,7 @@
 
 namespace kvp {
 
-enum SessionMode { MODE_INTRA = 0, MODE_CROSS = 1, MODE_STACK = 2 };
+enum SessionMode { MODE_INTRA = 0, MODE_CROSS = 1, MODE_STACK = 2, MODE_REUSE = 3 };
 
 struct SessionConfig {
     int mode;         // SessionMode
@@ -56,6 +63,8 @@ struct SessionStepInfo {
     int64_t map_rows;     // rows the kernel reads
     int64_t window_bytes; // persisting window span, 0 when none
     int64_t staged_bytes; // streaming: cumulative; dense: arena bytes used this step
+    int restaged;         // reuse: rows re-copied into a slot they already held
+    int hits;             // streaming: sticky hits (rows mapped without a copy)
 };
 
 class Session {
@@ -65,7 +74,9 @@ public:
     int status() const { return status_; }  // KVP_OK after construction
 
     // Host planning (no GPU needed).
-    int plan_frame(int f, const float* scores_flat);  // intra / cross
+    // intra / cross / reuse; reuse_flat ([frames][tiles], 1 = unchanged)
+    // is read in reuse mode only, NULL = every tile changed.
+    int plan_frame(int f, const float* scores_flat, const int8_t* reuse_flat = nullptr);
     int plan_stack(const float* scores_flat);         // stack
     const SessionStepInfo& info() const { return info_; }
     const int64_t* host_map() const { return map_.data(); }
@@ -90,9 +101,16 @@ public:
     // window when this step has no span).
     int apply_window(int layer, cudaStream_t s);
     int clear_window(cudaStream_t s);
+    // One per-frame step in a single call: plan_frame, then (unless the
+    // policy is None) upload, stage into every layer's arena and, when
+    // window_layer >= 0, the persisting window over that layer's arena.
+    int step(int f, const float* scores_flat, const int8_t* reuse_flat,
+             const void* const* k_layers, const void* const* v_layers, int window_layer,
+             cudaStream_t s);
 
 private:
     int stage_rows_of(int64_t gid, int64_t src_frame, int64_t tile);
+    int plan_reuse(int f, const float* scores_flat, const int8_t* reuse_flat);
 
     SessionConfig c_;
     TileLayout layout_;

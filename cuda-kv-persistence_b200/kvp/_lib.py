@@ -48,7 +48,8 @@ class SessionConfig(C.Structure):
 class StepInfo(C.Structure):
     _fields_ = [("frame", C.c_int), ("sel_count", C.c_int), ("staged_tiles", C.c_int),
                 ("copies", C.c_int), ("map_row0", C.c_longlong), ("map_rows", C.c_longlong),
-                ("window_bytes", C.c_longlong), ("staged_bytes", C.c_longlong)]
+                ("window_bytes", C.c_longlong), ("staged_bytes", C.c_longlong),
+                ("restaged", C.c_int), ("hits", C.c_int)]
 
 
 # name -> (restype, argtypes); every symbol include/*.h declares.
@@ -115,6 +116,9 @@ SIGNATURES = {
     "kvp_session_create": (C.c_void_p, [C.POINTER(SessionConfig)]),
     "kvp_session_destroy": (None, [C.c_void_p]),
     "kvp_session_plan_frame": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    "kvp_session_plan_frame_reuse": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "kvp_session_step": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p, C.c_int, C.c_void_p]),
     "kvp_session_plan_stack": (C.c_int, [C.c_void_p, C.c_void_p]),
     "kvp_session_finish": (C.c_int, [C.c_void_p]),
     "kvp_session_info": (C.c_int, [C.c_void_p, C.POINTER(StepInfo)]),

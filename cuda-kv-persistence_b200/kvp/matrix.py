@@ -4,10 +4,10 @@ trace, 30 layers, 5-frame causal window, ReuseWeighted).
 
 One cell is the reference driver's per-frame loop
 (src/run_policy_experiment.cu:156-274) for F frames x T tokens, one layer of
-H heads, bf16: for every frame f the Session selects, releases and stages the
-admitted tiles' rows into the arena, uploads the KVMap, sets the persisting
-window over the arena, and the tcgen05 kernel runs query frame f over key
-frames 0..f.  Everything is issued on one stream; unlike the reference there
+H heads, bf16: for every frame f one Session.step call selects, releases and
+stages the admitted tiles' rows into the arena, uploads the KVMap and sets
+the persisting window over the arena, and the tcgen05 kernel runs query
+frame f over key frames 0..f.  Everything is issued on one stream; unlike the reference there
 is no device synchronisation per frame.
 
 `cell_order` fixes the order of the cells (regime, budget, policy) and the
@@ -50,31 +50,33 @@ def cross_flops(frames: int, tokens: int, heads: int, head_dim: int = 128) -> fl
 
 
 def run_frames(q, k, v, out, scores, *, policy: str, set_aside: int, frames: int, tokens: int,
-               heads: int, stream: int, streaming: bool = False, events=None) -> dict:
+               heads: int, stream: int, streaming: bool = False, events=None,
+               mode: str = "cross") -> dict:
     """One pass over all frames of a cell.  The Session (device buffers) is
     created before and destroyed after the optional (start, end) CUDA events,
-    so a timed pass holds only the per-frame work."""
+    so a timed pass holds only the per-frame work.  mode "cross" (keys of
+    frames 0..f) or "intra" (keys of frame f)."""
     hidden = heads * 128
-    s = Session(mode="cross", policy=policy, frames=frames, tokens=tokens, hidden=hidden,
+    amode = "causal" if mode == "cross" else "intra"
+    s = Session(mode=mode, policy=policy, frames=frames, tokens=tokens, hidden=hidden,
                 elem_bytes=2, set_aside=set_aside, streaming=streaming, layers=1)
     copies = staged = 0
     try:
         if events:
             events[0].record()
+        kp, vp = [k.data_ptr()], [v.data_ptr()]
         for f in range(frames):
-            st = s.plan_frame(f, scores)
+            s.step(f, scores, kp, vp, window_layer=0, stream=stream)
+            st = s.info()
             copies += st.copies
             staged += st.staged_bytes
             if policy != "none":
-                s.upload(stream)
-                s.stage([k.data_ptr()], [v.data_ptr()], stream)
-                s.window(0, stream)
                 attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
-                          mode="causal", kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(0),
+                          mode=amode, kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(0),
                           arena_rows=s.cap_rows, stream=stream)
             else:
                 attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
-                          mode="causal", stream=stream)
+                          mode=amode, stream=stream)
         if policy != "none":
             s.clear_window(stream)
         if events:
@@ -84,6 +86,46 @@ def run_frames(q, k, v, out, scores, *, policy: str, set_aside: int, frames: int
     finally:
         s.close()
     return {"copies": copies, "staged_bytes": staged}
+
+
+def run_reuse_frames(q, k, v, out, scores, reuse, *, policy: str, set_aside: int, frames: int,
+                     tokens: int, heads: int, stream: int, events=None) -> dict:
+    """Temporal-reuse pass: per frame f the Session (mode "reuse") selects
+    among frame f's tiles, keeps the slots of tiles it keeps selecting, and
+    stages only new or changed tiles' rows; the kernel runs frame f's
+    queries over frame f's keys through the KVMap (intra).  A kept,
+    unchanged tile is read from the slot written in an earlier frame."""
+    hidden = heads * 128
+    s = Session(mode="reuse", policy=policy, frames=frames, tokens=tokens, hidden=hidden,
+                elem_bytes=2, set_aside=set_aside, streaming=True, layers=1)
+    tot = {"copies": 0, "restaged": 0, "hits": 0, "staged_bytes": 0}
+    try:
+        if events:
+            events[0].record()
+        kp, vp = [k.data_ptr()], [v.data_ptr()]
+        for f in range(frames):
+            s.step(f, scores, kp, vp, reuse=reuse, window_layer=0, stream=stream)
+            st = s.info()
+            tot["copies"] += st.copies
+            tot["restaged"] += st.restaged
+            tot["hits"] += st.hits
+            tot["staged_bytes"] = st.staged_bytes
+            if policy != "none":
+                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
+                          mode="intra", kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(0),
+                          arena_rows=s.cap_rows, stream=stream)
+            else:
+                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
+                          mode="intra", stream=stream)
+        if policy != "none":
+            s.clear_window(stream)
+        if events:
+            events[1].record()
+        torch.cuda.synchronize()
+        s.finish()
+    finally:
+        s.close()
+    return tot
 
 
 def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: int = 12,
@@ -257,4 +299,86 @@ def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: i
                     "ms_runs": [round(x, 3) for x in ts],
                     "tflops": round(flops / (t / 1e3) / 1e12, 2), "flop": flops,
                     "device_status": read_status()})
+    return res
+
+
+def run_reuse_matrix(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: int = 12,
+                     seed: int = 0, max_persist: int | None = None, device="cuda") -> list[dict]:
+    """Temporal reuse against re-staging every frame, per (trace, budget,
+    policy): intra attention per frame on K/V whose unchanged tiles hold the
+    previous frame's rows.  Legs: "none" (no map), "dense" (dense arena, every
+    admitted row copied every frame, the reference's staging), "reuse"
+    (Session mode reuse).  Every leg's output must equal None's bitwise.
+    Traces: AR(1) rho 0.9 (BASELINE config 2's motion model, temporally
+    coherent) and config 5 'high' (i.i.d. per frame); reuse flags by the
+    percentile-50 rule."""
+    from ._lib import DeviceInfo, lib
+    from .traces import hold_reused_tiles, reuse_flags
+    import ctypes as C
+    if max_persist is None:
+        info = DeviceInfo()
+        lib().kvp_query_device(-1, C.byref(info))
+        max_persist = int(info.max_persisting_l2_bytes)
+    hidden = heads * 128
+    nt = (tokens + 15) // 16
+    traces = {"ar1": motion_config2(frames=frames, seed=seed, tiles=nt),
+              "iid": motion_config5("high", frames=frames, seed=seed, tiles=nt)}
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    flops = float(4 * tokens * tokens * 128 * frames * heads)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    res = []
+    for name, scores in traces.items():
+        reuse = reuse_flags(scores)
+        q, k, v = qkv(frames * tokens, hidden, seed=seed)
+        hold_reused_tiles(k, v, reuse, tokens=tokens)
+        q, k, v = q.to(device), k.to(device), v.to(device)
+        out = torch.empty_like(q)
+        ref = torch.empty_like(q)
+
+        def leg(kind, policy, sa, events=None):
+            if kind == "reuse":
+                return run_reuse_frames(q, k, v, out, scores, reuse, policy=policy, set_aside=sa,
+                                        frames=frames, tokens=tokens, heads=heads, stream=stream,
+                                        events=events)
+            st = run_frames(q, k, v, out, scores, policy=policy, set_aside=sa, frames=frames,
+                            tokens=tokens, heads=heads, stream=stream, events=events,
+                            mode="intra")
+            return {"copies": st["copies"], "staged_bytes": st["staged_bytes"], "hits": 0,
+                    "restaged": 0}
+
+        read_status()
+        leg("dense", "none", 0)
+        ref.copy_(out)
+        cells = [("none", "none", 0)]
+        for frac in BUDGET_FRACS:
+            for policy in POLICY_ORDER[1:]:
+                for kind in ("dense", "reuse"):
+                    cells.append((kind, policy, int(frac * max_persist)))
+        counters = {}
+        for c in cells:                       # warm-up + bitwise gate
+            counters[c] = leg(*c)
+            if not torch.equal(out, ref):
+                raise RuntimeError(f"reuse matrix: {name} {c} differs from the None policy")
+        times = {c: [] for c in cells}
+        order = []
+        for r in range(reps):
+            order += cells if r % 2 == 0 else cells[::-1]
+        for c in order:
+            leg(*c, events=(e0, e1))
+            times[c].append(e0.elapsed_time(e1))
+        status = read_status()
+        for c in cells:
+            t = np.array(times[c])
+            kind, policy, sa = c
+            cnt = counters[c]
+            copied = cnt["copies"] * 2 * hidden * 2
+            res.append({"trace": name, "leg": kind, "policy": policy, "set_aside_bytes": sa,
+                        "budget_frac": round(sa / max_persist, 2) if max_persist else 0,
+                        "rows_copied": cnt["copies"], "bytes_copied": copied,
+                        "rows_restaged": cnt["restaged"], "sticky_hits": cnt["hits"],
+                        "ms_mean": round(float(t.mean()), 4),
+                        "cv_pct": round(float(100 * t.std(ddof=1) / t.mean()) if len(t) > 1 else 0.0, 3),
+                        "tflops": round(flops / (t.mean() / 1e3) / 1e12, 2), "reps": len(t),
+                        "device_status": status})
     return res

@@ -15,7 +15,7 @@ import numpy as np
 from ._lib import KvpError, SessionConfig, StepInfo, check, lib
 from .policies import POLICIES
 
-MODES = {"intra": 0, "cross": 1, "stack": 2}
+MODES = {"intra": 0, "cross": 1, "stack": 2, "reuse": 3}
 
 
 @dataclass
@@ -28,6 +28,8 @@ class Step:
     map_rows: int
     window_bytes: int
     staged_bytes: int
+    restaged: int = 0
+    hits: int = 0
 
 
 class Session:
@@ -61,9 +63,17 @@ class Session:
     def cap_rows(self) -> int:
         return int(self._L.kvp_session_cap_rows(self.h))
 
-    def plan_frame(self, frame: int, scores_flat: np.ndarray) -> Step:
+    def plan_frame(self, frame: int, scores_flat: np.ndarray, reuse=None) -> Step:
+        """reuse ([frames][tiles] int8, 1 = tile unchanged) is read in reuse
+        mode only; None = every tile changed."""
         s = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
-        check(self._L.kvp_session_plan_frame(self.h, frame, s.ctypes.data), "plan_frame")
+        if self.mode == "reuse":
+            r = None if reuse is None else np.ascontiguousarray(reuse, dtype=np.int8).reshape(-1)
+            check(self._L.kvp_session_plan_frame_reuse(self.h, frame, s.ctypes.data,
+                                                       None if r is None else r.ctypes.data),
+                  "plan_frame")
+        else:
+            check(self._L.kvp_session_plan_frame(self.h, frame, s.ctypes.data), "plan_frame")
         return self.info()
 
     def plan_stack(self, scores_flat: np.ndarray) -> Step:
@@ -78,7 +88,7 @@ class Session:
         i = StepInfo()
         check(self._L.kvp_session_info(self.h, C.byref(i)), "info")
         return Step(i.frame, i.sel_count, i.staged_tiles, i.copies, i.map_row0, i.map_rows,
-                    i.window_bytes, i.staged_bytes)
+                    i.window_bytes, i.staged_bytes, i.restaged, i.hits)
 
     def host_map(self, row0: int = 0, n: int | None = None) -> np.ndarray:
         n = self.map_len - row0 if n is None else n
@@ -117,6 +127,22 @@ class Session:
     def stage_layer(self, layer: int, k_ptr: int, v_ptr: int, stream: int = 0):
         check(self._L.kvp_session_stage_layer(self.h, layer, C.c_void_p(k_ptr), C.c_void_p(v_ptr),
                                               C.c_void_p(stream)), "stage_layer")
+
+    def step(self, frame: int, scores_flat: np.ndarray, k_ptrs, v_ptrs, *, reuse=None,
+             window_layer: int = 0, stream: int = 0):
+        """plan_frame + upload + stage + window(window_layer) in one native
+        call (only plan_frame for the None policy); window_layer < 0 skips
+        the window.  Read info() for the step's counters."""
+        s = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
+        r = None
+        if reuse is not None and self.mode == "reuse":
+            r = np.ascontiguousarray(reuse, dtype=np.int8).reshape(-1)
+        n = len(k_ptrs)
+        ka = (C.c_void_p * max(n, 1))(*k_ptrs)
+        va = (C.c_void_p * max(n, 1))(*v_ptrs)
+        check(self._L.kvp_session_step(self.h, frame, s.ctypes.data,
+                                       None if r is None else r.ctypes.data, ka, va, window_layer,
+                                       C.c_void_p(stream)), "step")
 
     def window(self, layer: int, stream: int = 0):
         check(self._L.kvp_session_window(self.h, layer, C.c_void_p(stream)), "window")

@@ -68,32 +68,55 @@ def reference_synthetic_trace(frames: int = 8, seed: int = 42, frac_static: floa
     return scores.numpy(), is_static.numpy(), q.numpy(), k.numpy(), v.numpy()
 
 
+def reuse_flags(scores: np.ndarray, percentile: float = 50.0) -> np.ndarray:
+    """The CSV reuse column from per-tile change rates [frames][tiles]:
+    1 where the rate is below the `percentile`-th percentile of frames 1..F-1
+    (linear interpolation), frame 0 always 0 (written fresh).  The rule of
+    traces/gen_motion_from_video.py:118-122, whose motion_score is that
+    change rate."""
+    s = np.asarray(scores, dtype=np.float64)
+    reuse = np.zeros(s.shape, dtype=np.int8)
+    if s.shape[0] > 1:
+        tau = float(np.percentile(s[1:], percentile))
+        reuse[1:] = (s[1:] < tau).astype(np.int8)
+    return reuse
+
+
 def write_motion_csv(path, scores: np.ndarray, is_static=None, tokens: int = TOKENS,
-                     tile_tokens: int = TILE) -> Path:
+                     tile_tokens: int = TILE, reuse=None) -> Path:
+    """Reference trace CSV; with `reuse` ([frames][tiles]) the optional 7th
+    column of traces/gen_motion_from_video.py is written too."""
     scores = np.asarray(scores, dtype=np.float32)
     frames, n = scores.shape
     counts = tile_counts(tokens, tile_tokens)
     starts = np.cumsum(counts) - counts
     if is_static is None:
         is_static = np.zeros(n, dtype=bool)
-    lines = ["frame_id,tile_id,motion_score,is_static,token_start,token_count"]
+    head = "frame_id,tile_id,motion_score,is_static,token_start,token_count"
+    lines = [head + (",reuse" if reuse is not None else "")]
     for f in range(frames):
         for t in range(n):
-            lines.append(f"{f},{t},{float(scores[f, t]):.6f},{int(is_static[t])},"
-                         f"{int(starts[t])},{int(counts[t])}")
+            row = (f"{f},{t},{float(scores[f, t]):.6f},{int(is_static[t])},"
+                   f"{int(starts[t])},{int(counts[t])}")
+            if reuse is not None:
+                row += f",{int(reuse[f][t])}"
+            lines.append(row)
     p = Path(path)
     p.write_text("\n".join(lines) + "\n")
     return p
 
 
-def read_motion_csv(path, frames: int, num_tiles: int) -> np.ndarray:
-    """Scores exactly as the reference parses them (sscanf %f), via the C ABI."""
+def read_motion_csv(path, frames: int, num_tiles: int, with_reuse: bool = False):
+    """Scores exactly as the reference parses them (sscanf %f), via the C ABI;
+    with_reuse also returns the reuse column (int8, 0 where absent)."""
     from ._lib import lib
     s = np.zeros((frames, num_tiles), dtype=np.float32)
-    n = lib().kvp_read_motion_csv(str(path).encode(), frames, num_tiles, s.ctypes.data, None)
+    r = np.zeros((frames, num_tiles), dtype=np.int8)
+    n = lib().kvp_read_motion_csv(str(path).encode(), frames, num_tiles, s.ctypes.data,
+                                  r.ctypes.data if with_reuse else None)
     if n < 0:
         raise FileNotFoundError(path)
-    return s
+    return (s, r) if with_reuse else s
 
 
 def csv_round_trip(scores: np.ndarray, workdir) -> np.ndarray:
@@ -159,3 +182,17 @@ def qkv(rows: int, hidden: int = HIDDEN, *, seed: int = 0, dtype=torch.bfloat16,
         t = torch.randn(rows, hidden, generator=g, device=device, dtype=torch.float32) * s
         out.append(t.to(dtype))
     return tuple(out)
+
+
+def hold_reused_tiles(k: torch.Tensor, v: torch.Tensor, reuse: np.ndarray, *, tokens: int = TOKENS,
+                      tile_tokens: int = TILE) -> None:
+    """In place: the rows of every tile flagged unchanged in frame f (reuse
+    [frames][tiles] == 1) become copies of frame f-1's rows, i.e. K/V as a
+    model that skips recomputing static tiles would hold them."""
+    frames, nt = np.asarray(reuse).shape
+    for f in range(1, frames):
+        for t in np.nonzero(np.asarray(reuse)[f])[0]:
+            a = f * tokens + int(t) * tile_tokens
+            b = min(a + tile_tokens, (f + 1) * tokens)
+            k[a:b] = k[a - tokens:b - tokens]
+            v[a:b] = v[a - tokens:b - tokens]

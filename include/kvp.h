@@ -117,7 +117,10 @@ int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d,
 /* ---- Session: the per-frame admission loop / KVMap emitter of
  * src/run_policy_experiment.cu:156-274 as a library. */
 typedef struct {
-    int mode;        /* 0 intra, 1 cross, 2 stack (one admission for all frames) */
+    int mode;        /* 0 intra, 1 cross, 2 stack (one admission for all frames),
+                        3 reuse (intra attention; streaming slots keyed by token
+                        position, re-copied only when the tile changed; needs
+                        streaming = 1) */
     int window;      /* cross: 0 = full prefix, W = candidates of the last W frames */
     int streaming;   /* 0 dense arena, 1 sticky streaming slots */
     int policy;      /* as tgp_select */
@@ -130,12 +133,21 @@ typedef struct {
 typedef struct {
     int frame, sel_count, staged_tiles, copies;
     long long map_row0, map_rows, window_bytes, staged_bytes;
+    int restaged;    /* reuse mode: rows re-copied into a slot they held */
+    int hits;        /* streaming: rows mapped to a held slot without a copy */
 } kvp_step_info;
 
 void* kvp_session_create(const kvp_session_config* c);
 void kvp_session_destroy(void* s);
 int kvp_session_plan_frame(void* s, int frame, const float* scores_flat); /* intra / cross */
 int kvp_session_plan_stack(void* s, const float* scores_flat);            /* stack */
+/* Reuse mode (no reference counterpart: the reference reads the motion
+ * CSV's reuse column, src/run_policy_experiment.cu:114-118, and stages with
+ * changed = false, :211).  reuse_flat is [frames][tiles], 1 = tile unchanged
+ * since the previous frame; NULL = every tile changed.  A selected,
+ * unchanged tile whose rows hold slots copies nothing. */
+int kvp_session_plan_frame_reuse(void* s, int frame, const float* scores_flat,
+                                 const signed char* reuse_flat);
 int kvp_session_finish(void* s);
 int kvp_session_info(void* s, kvp_step_info* out);
 long long kvp_session_slots(void* s);
@@ -151,6 +163,15 @@ int kvp_session_stage(void* s, const void* const* k_layers, const void* const* v
 int kvp_session_stage_layer(void* s, int layer, const void* k, const void* v, void* stream);
 int kvp_session_window(void* s, int layer, void* stream);
 int kvp_session_clear_window(void* s, void* stream);
+/* One per-frame step in one call (no reference counterpart; the reference
+ * driver does these steps inline, src/run_policy_experiment.cu:156-274):
+ * kvp_session_plan_frame_reuse (reuse_flat is read in reuse mode only),
+ * then, unless the policy is None, kvp_session_upload, kvp_session_stage and,
+ * when window_layer >= 0, kvp_session_window(window_layer).  Stops at the
+ * first error and returns it. */
+int kvp_session_step(void* s, int frame, const float* scores_flat, const signed char* reuse_flat,
+                     const void* const* k_layers, const void* const* v_layers, int window_layer,
+                     void* stream);
 
 #ifdef __cplusplus
 }

@@ -481,3 +481,92 @@ int orc_run_trace(const orc_params* p, const float* scores_flat, int64_t* map_ou
     orc_mgr_destroy(m);
     return rc;
 }
+
+/* ------------------------------------------------- temporal-reuse streaming */
+int orc_run_reuse(const orc_params* p, const float* scores_flat, const int8_t* reuse_flat,
+                  int64_t* map_out, int* copy_count, int* restage_count, int* hit_count,
+                  int64_t* copy_rows, int64_t* copy_slots, int64_t copy_cap,
+                  int64_t* window_bytes, int64_t* staged_bytes, int* staged_tiles) {
+    /* src/run_policy_experiment.cu:156-274 (intra, streaming) with position
+     * keys and changed = !reuse; src/kv_tile_manager.cu:153-200 */
+    if (!p || !p->streaming || p->cross || p->frames <= 0 || p->tokens <= 0 || p->hidden <= 0 ||
+        p->tile_tokens <= 0 || p->elem_bytes <= 0 || (2 * p->hidden * p->elem_bytes) % 4 != 0)
+        return -1;
+    const int F = p->frames, T = p->tokens, tt = p->tile_tokens;
+    const int64_t nt = orc_tiles_per_frame(T, tt);
+    for (int f = 0; f < F; ++f) {
+        copy_count[f] = restage_count[f] = hit_count[f] = 0;
+        window_bytes[f] = -1; staged_bytes[f] = 0; staged_tiles[f] = 0;
+    }
+    for (size_t i = 0; i < (size_t)F * (size_t)T; ++i) map_out[i] = -1;
+    if (p->policy == ORC_NONE) return 0;
+
+    const uint64_t row_kv_bytes = (uint64_t)p->hidden * (uint64_t)p->elem_bytes;
+    const uint64_t tile_bytes = (uint64_t)tt * row_kv_bytes * 2u;
+    const int64_t slots = (int64_t)((uint64_t)p->set_aside / tile_bytes);
+    orc_mgr* m = orc_mgr_create(p->set_aside, p->set_aside);
+    if (!m) return -3;
+    orc_mgr_init(m);
+    orc_mgr_arena_init(m, p->set_aside, (int64_t)(2u * row_kv_bytes / 4u));
+    int64_t* ids = (int64_t*)malloc(sizeof(int64_t) * (size_t)(slots + nt + 1));
+    char* selected = (char*)calloc((size_t)nt + 1, 1);
+    char* prev_sel = (char*)calloc((size_t)nt + 1, 1);
+    int rc = 0;
+    int64_t n_copies = 0;
+    orc_mgr_streaming_begin(m);
+
+    for (int f = 0; f < F && rc == 0; ++f) {
+        int count = 0;
+        orc_select(p->policy, scores_flat + (int64_t)f * nt, (int)nt, (int)slots, (int)nt, F, ids,
+                   &count);
+        memset(selected, 0, (size_t)nt);
+        for (int i = 0; i < count; ++i)
+            if (ids[i] >= 0 && ids[i] < nt) selected[ids[i]] = 1;
+        if (f > 0) {
+            for (int64_t tile = 0; tile < nt; ++tile) {
+                if (!prev_sel[tile] || selected[tile]) continue;
+                const int64_t t0 = tile * tt;
+                const int64_t c = (T - t0) < tt ? (T - t0) : tt;
+                /* last row first: the LIFO free stack then hands the
+                 * tile's slots back in ascending order */
+                for (int64_t r = c - 1; r >= 0; --r) orc_mgr_streaming_release(m, t0 + r);
+            }
+        }
+        int64_t* h_map = map_out + (size_t)f * (size_t)T;
+        int tiles_ok = 0;
+        for (int i = 0; i < count; ++i) {
+            if (ids[i] < 0 || ids[i] >= nt) continue;
+            const int64_t tile = ids[i];
+            const int64_t t0 = tile * tt;
+            const int64_t c = (T - t0) < tt ? (T - t0) : tt;
+            const int changed = !(reuse_flat && reuse_flat[(size_t)f * (size_t)nt + (size_t)tile]);
+            int all = 1;
+            for (int64_t r = 0; r < c && all; ++r) {
+                int64_t slot = -1, had = -1;
+                int copied = 0;
+                const int held = hm_find(&m->row_slot, t0 + r, &had);
+                all = orc_mgr_streaming_stage(m, t0 + r, (int64_t)row_kv_bytes,
+                                              (int64_t)row_kv_bytes, changed, &slot, &copied);
+                if (!all) break;
+                h_map[t0 + r] = slot;
+                if (!copied) { ++hit_count[f]; continue; }
+                if (held) ++restage_count[f];
+                if (n_copies >= copy_cap) { rc = -4; break; }
+                copy_rows[n_copies] = (int64_t)f * T + t0 + r;
+                copy_slots[n_copies] = slot;
+                ++n_copies;
+                ++copy_count[f];
+            }
+            if (rc) break;
+            if (all) ++tiles_ok;
+        }
+        staged_tiles[f] = tiles_ok;
+        window_bytes[f] = orc_mgr_streaming_window(m) ? orc_mgr_last_window_bytes(m) : -1;
+        staged_bytes[f] = orc_mgr_streaming_staged_bytes(m);
+        memcpy(prev_sel, selected, (size_t)nt);
+    }
+    orc_mgr_streaming_end(m);
+    free(ids); free(selected); free(prev_sel);
+    orc_mgr_destroy(m);
+    return rc;
+}

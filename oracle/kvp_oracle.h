@@ -94,6 +94,30 @@ int orc_run_trace(const orc_params* p, const float* scores_flat, int64_t* map_ou
                   int64_t* copy_rows, int64_t* copy_slots, int64_t copy_cap,
                   int64_t* window_bytes, int64_t* staged_bytes, int* staged_tiles);
 
+/* Temporal-reuse streaming loop (intra attention, streaming manager).  The
+ * reference's loop (src/run_policy_experiment.cu:156-274) with two changes:
+ * a row's slot key is its token position t0+r, not frame*tokens+t0+r, so a
+ * tile's slots outlive the frame; and streaming_stage gets changed =
+ * !reuse[f][tile] (the CSV reuse column, 1 = tile unchanged since the
+ * previous frame; NULL = every tile changed) instead of the constant false
+ * of :211.  A sticky hit on an unchanged tile copies nothing; a changed
+ * tile is re-copied into the slot it holds (src/kv_tile_manager.cu:153-175).
+ * Tiles selected at f-1 and not at f release their position keys first,
+ * last row first, so that slots come back off the LIFO free stack
+ * (src/kv_tile_manager.cu:194-200) in ascending order.
+ * Outputs (caller-allocated):
+ *   map_out       [frames][tokens]   frame f's KVMap (absolute row f*tokens+t)
+ *   copy_count    [frames]           rows copied this frame (new + restaged)
+ *   restage_count [frames]           rows re-copied into a slot they held
+ *   hit_count     [frames]           sticky hits (no copy)
+ *   copy_rows / copy_slots [copy_cap] (source row -> slot), concatenated
+ *   window_bytes / staged_bytes / staged_tiles [frames] as orc_run_trace.
+ * Requires p->streaming and !p->cross.  Returns 0 or < 0. */
+int orc_run_reuse(const orc_params* p, const float* scores_flat, const int8_t* reuse_flat,
+                  int64_t* map_out, int* copy_count, int* restage_count, int* hit_count,
+                  int64_t* copy_rows, int64_t* copy_slots, int64_t copy_cap,
+                  int64_t* window_bytes, int64_t* staged_bytes, int* staged_tiles);
+
 #ifdef __cplusplus
 }
 #endif

@@ -92,6 +92,8 @@ class Oracle:
         L.orc_run_trace.argtypes = [C.POINTER(_OrcParams), f32p, i64p, i32p, i64p, C.c_int,
                                     i32p, i64p, i64p, C.c_int64, i64p, i64p, i32p]
         L.orc_read_motion_csv.argtypes = [C.c_char_p, C.c_int, C.c_int, f32p, C.c_void_p]
+        L.orc_run_reuse.argtypes = [C.POINTER(_OrcParams), f32p, C.c_void_p, i64p, i32p, i32p,
+                                    i32p, i64p, i64p, C.c_int64, i64p, i64p, i32p]
         L.orc_tiles_per_frame.restype = C.c_int64
         L.orc_tile_start.restype = C.c_int64
         L.orc_tile_start.argtypes = [C.c_int, C.c_int, C.c_int64]
@@ -130,11 +132,13 @@ class Oracle:
         assert rc == 0
         return out[:cnt.value].copy()
 
-    def read_motion_csv(self, path, frames, num_tiles):
+    def read_motion_csv(self, path, frames, num_tiles, with_reuse=False):
         s = np.zeros((frames, num_tiles), dtype=np.float32)
-        n = self.L.orc_read_motion_csv(str(path).encode(), frames, num_tiles, s.reshape(-1), None)
+        r = np.zeros((frames, num_tiles), dtype=np.int8)
+        n = self.L.orc_read_motion_csv(str(path).encode(), frames, num_tiles, s.reshape(-1),
+                                       r.ctypes.data if with_reuse else None)
         assert n >= 0, f"cannot read {path}"
-        return s
+        return (s, r) if with_reuse else s
 
     def run_trace(self, scores_flat, *, policy, cross, streaming, frames, tokens=1560,
                   hidden=1536, tile_tokens=16, elem_bytes=4, window=0, set_aside=2162688):
@@ -166,6 +170,34 @@ class Oracle:
                            copy_slots[:n].copy(), window_bytes, staged_bytes, staged_tiles)
 
     # manager (accounting restatement) -----------------------------------
+    def run_reuse(self, scores_flat, reuse_flat, *, policy, frames, tokens=1560, hidden=1536,
+                  tile_tokens=16, elem_bytes=4, set_aside=2162688) -> dict:
+        """Temporal-reuse streaming loop (kvp_oracle.c orc_run_reuse)."""
+        p = _OrcParams(POLICIES[policy], 0, 1, frames, tokens, hidden, tile_tokens, elem_bytes, 0,
+                       set_aside)
+        nt = (tokens + tile_tokens - 1) // tile_tokens
+        cap_rows = set_aside // (2 * hidden * elem_bytes)
+        copy_cap = max(frames * cap_rows, 1)
+        scores = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
+        assert scores.size >= frames * nt
+        reuse = None
+        if reuse_flat is not None:
+            reuse = np.ascontiguousarray(reuse_flat, dtype=np.int8).reshape(-1)
+            assert reuse.size >= frames * nt
+        out = {k: np.zeros(frames, np.int32) for k in ("copies", "restaged", "hits", "staged_tiles")}
+        out.update({k: np.zeros(frames, np.int64) for k in ("window_bytes", "staged_bytes")})
+        maps = np.empty((frames, tokens), np.int64)
+        copy_rows = np.zeros(copy_cap, np.int64)
+        copy_slots = np.zeros(copy_cap, np.int64)
+        rc = self.L.orc_run_reuse(C.byref(p), scores, None if reuse is None else reuse.ctypes.data,
+                                  maps.reshape(-1), out["copies"], out["restaged"], out["hits"],
+                                  copy_rows, copy_slots, copy_cap, out["window_bytes"],
+                                  out["staged_bytes"], out["staged_tiles"])
+        assert rc == 0, f"orc_run_reuse rc={rc}"
+        n = int(out["copies"].sum())
+        out.update(maps=maps, copy_rows=copy_rows[:n].copy(), copy_slots=copy_slots[:n].copy())
+        return out
+
     def manager(self, budget, max_window):
         return _OrcMgr(self.L, budget, max_window)
 
@@ -226,6 +258,8 @@ class RefLib:
                                            C.c_void_p, C.c_long, C.c_int, C.POINTER(C.c_long),
                                            C.POINTER(C.c_int)]
         L.kvtm_streaming_release.argtypes = [C.c_void_p, C.c_long]
+        L.kvpref_run_reuse.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_long,
+                                       f32p, C.c_void_p, i64p, i32p, i32p, i32p, i64p, i64p]
         L.kvtm_layout_tiles_per_frame.restype = C.c_long
         L.kvtm_layout_tiles_per_frame.argtypes = [C.c_int, C.c_int]
         L.kvtm_layout_tile_start.restype = C.c_long
@@ -251,6 +285,23 @@ class RefLib:
                                       staged)
         assert rc == 0, rc
         return maps, staged
+
+    def run_reuse(self, scores_flat, reuse_flat, *, policy, frames, tokens=1560, hidden=1536,
+                  tile_tokens=16, set_aside=2162688) -> dict:
+        """The reference's KVTileManager driven by the temporal-reuse loop of
+        ref_stub/ref_shims.cpp (kvpref_run_reuse); fp32 accounting."""
+        s = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
+        r = None if reuse_flat is None else np.ascontiguousarray(reuse_flat, dtype=np.int8).reshape(-1)
+        maps = np.empty((frames, tokens), np.int64)
+        out = {k: np.zeros(frames, np.int32) for k in ("copies", "restaged", "hits")}
+        out.update({k: np.zeros(frames, np.int64) for k in ("staged_bytes", "window_bytes")})
+        rc = self.L.kvpref_run_reuse(POLICIES[policy], frames, tokens, hidden, tile_tokens, set_aside,
+                                     s, None if r is None else r.ctypes.data, maps.reshape(-1),
+                                     out["copies"], out["restaged"], out["hits"], out["staged_bytes"],
+                                     out["window_bytes"])
+        assert rc == 0, rc
+        out["maps"] = maps
+        return out
 
 
 @dataclass

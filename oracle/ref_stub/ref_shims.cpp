@@ -123,3 +123,91 @@ extern "C" int kvpref_run_window(int policy, int streaming, int window, int fram
     cudaFree(d_v);
     return 0;
 }
+
+// Temporal-reuse streaming loop over the reference's KVTileManager: intra
+// candidates (one frame's tiles), slot keys = token position t0+r, and
+// streaming_stage(changed = !reuse[f][tile]) -- the reference driver always
+// passes false (src/run_policy_experiment.cu:211).  Per frame: map_out
+// [frames][tokens], copies (restaged == true), restaged (copies into a slot
+// the key already held, tracked here), hits, staged bytes, window bytes
+// (-1 when the window was refused).
+#include <unordered_set>
+
+extern "C" size_t kvpref_last_window_bytes(void);
+
+extern "C" int kvpref_run_reuse(int policy, int frames, int tokens, int hidden, int tile_tokens,
+                                long set_aside, const float* scores_flat,
+                                const signed char* reuse_flat, long* map_out, int* copies_out,
+                                int* restaged_out, int* hits_out, long* staged_out,
+                                long* window_out) {
+    const long num_tiles = (tokens + tile_tokens - 1) / tile_tokens;
+    const size_t elems = (size_t)frames * tokens * hidden;
+    float* d_k = nullptr;
+    float* d_v = nullptr;
+    if (cudaMalloc(&d_k, elems * 4) != cudaSuccess) return -1;
+    if (cudaMalloc(&d_v, elems * 4) != cudaSuccess) return -1;
+    KVTileManager mgr((size_t)set_aside, (size_t)set_aside);
+    const size_t tile_bytes = (size_t)tile_tokens * hidden * 4 * 2;
+    const long slots = (long)(set_aside / tile_bytes);
+    if (!mgr.init() || !mgr.arena_init((size_t)set_aside, (size_t)hidden * 2)) return -2;
+    std::unique_ptr<TileGatingPolicy> pol(make_policy(policy, (int)num_tiles, frames));
+    if (!pol) return -3;
+    std::vector<long> ids((size_t)num_tiles + (size_t)slots + 1);
+    std::vector<char> prev_selected((size_t)num_tiles, 0);
+    std::unordered_set<long> held;
+    for (size_t i = 0; i < (size_t)frames * tokens; ++i) map_out[i] = -1;
+    const bool persist = policy != 0;
+    if (persist) mgr.streaming_begin();
+    for (long f = 0; f < frames; ++f) {
+        copies_out[f] = restaged_out[f] = hits_out[f] = 0;
+        staged_out[f] = 0;
+        window_out[f] = -1;
+        if (!persist) continue;
+        int count = 0;
+        pol->select(scores_flat + f * num_tiles, (int)num_tiles, (int)slots, ids.data(), &count);
+        std::vector<char> selected((size_t)num_tiles, 0);
+        for (int i = 0; i < count; ++i)
+            if (ids[i] >= 0 && ids[i] < num_tiles) selected[(size_t)ids[i]] = 1;
+        if (f > 0) {
+            for (long tile = 0; tile < num_tiles; ++tile) {
+                if (!prev_selected[tile] || selected[tile]) continue;
+                const long t0 = tile * tile_tokens;
+                const long c = std::min((long)tile_tokens, (long)tokens - t0);
+                for (long r = c - 1; r >= 0; --r)   // last row first: slots pop ascending
+                    if (mgr.streaming_release(t0 + r)) held.erase(t0 + r);
+            }
+        }
+        long* h_map = map_out + f * tokens;
+        for (int i = 0; i < count; ++i) {
+            if (ids[i] < 0 || ids[i] >= num_tiles) continue;
+            const long tile = ids[i];
+            const long t0 = tile * tile_tokens;
+            const long c = std::min((long)tile_tokens, (long)tokens - t0);
+            const bool changed = !(reuse_flat && reuse_flat[f * num_tiles + tile]);
+            bool all = true;
+            for (long r = 0; r < c && all; ++r) {
+                const long row_id = f * tokens + t0 + r;
+                long slot = -1;
+                bool restaged = false;
+                const bool was_held = held.count(t0 + r) != 0;
+                all = mgr.streaming_stage(t0 + r, d_k + (size_t)row_id * hidden,
+                                          (size_t)hidden * 4, d_v + (size_t)row_id * hidden,
+                                          (size_t)hidden * 4, changed, &slot, &restaged);
+                if (!all) break;
+                held.insert(t0 + r);
+                h_map[t0 + r] = slot;
+                if (!restaged) { ++hits_out[f]; continue; }
+                ++copies_out[f];
+                if (was_held) ++restaged_out[f];
+            }
+        }
+        if (mgr.streaming_apply_window())
+            window_out[f] = (long)kvpref_last_window_bytes();
+        staged_out[f] = (long)mgr.streaming_staged_bytes();
+        prev_selected = selected;
+    }
+    if (persist) mgr.streaming_end();
+    cudaFree(d_k);
+    cudaFree(d_v);
+    return 0;
+}

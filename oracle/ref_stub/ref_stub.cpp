@@ -19,6 +19,7 @@ static FILE* g_log = nullptr;
 static bool g_log_init = false;
 static size_t g_limit = 0;
 static long g_alloc_idx = 0;
+static size_t g_last_window = 0;
 
 static FILE* logf_() {
     if (!g_log_init) {
@@ -82,6 +83,7 @@ cudaError_t cudaDeviceGetLimit(size_t* v, cudaLimit) {
 
 cudaError_t cudaStreamSetAttribute(cudaStream_t, cudaStreamAttrID,
                                    const cudaStreamAttrValue* v) {
+    g_last_window = v->accessPolicyWindow.num_bytes;
     if (FILE* f = logf_())
         fprintf(f, "W %llu %zu %d\n",
                 (unsigned long long)(uintptr_t)v->accessPolicyWindow.base_ptr,
@@ -101,6 +103,9 @@ cudaError_t cudaDeviceReset(void) {
     return cudaSuccess;
 }
 const char* cudaGetErrorString(cudaError_t) { return "stub"; }
+
+// num_bytes of the last access-policy window set on a stream.
+size_t kvpref_last_window_bytes(void) { return g_last_window; }
 
 }  // extern "C"
 

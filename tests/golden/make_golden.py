@@ -1,6 +1,6 @@
 """Regenerates the committed golden fixtures from the reference's own code.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref /root/reference] [--only reuse]
 
 Needs the reference sources (read, never copied) and is run once, on a host
 where they exist; the tests only read the files it writes:
@@ -24,6 +24,12 @@ where they exist; the tests only read the files it writes:
 * ``reference_meta.json`` numbers the reference ships as text for the seed-42
                           8-frame trace (traces/trace_meta_8f.json tile counts
                           and cosines, traces/golden_meta.json per-frame stats).
+* ``kvmap_reuse_ref.json`` the temporal-reuse streaming loop (slots keyed by
+                          token position, changed = !reuse) run on the
+                          reference's KVTileManager through the shims, with
+                          ``motion_config2_reuse.csv`` (a trace carrying the
+                          optional reuse column).  ``--only reuse`` rewrites
+                          just these two files.
 """
 
 from __future__ import annotations
@@ -90,12 +96,64 @@ def oracle_case(scores, *, policy, mode, streaming, frames, set_aside, window=0)
     return out, int(res.staged_bytes[-1]) if streaming else None
 
 
+def reuse_fixtures():
+    """kvmap_reuse_ref.json: the temporal-reuse streaming loop run on the
+    reference's own KVTileManager (oracle/ref_stub/ref_shims.cpp
+    kvpref_run_reuse), per frame: KVMap digest, copies, re-copies into held
+    slots, sticky hits, cumulative staged bytes, window bytes.  The oracle's
+    restatement must agree before anything is written."""
+    from kvp import traces
+    R, O = orc.RefLib(), orc.Oracle()
+    sc2 = traces.motion_config2()
+    traces.write_motion_csv(HERE / "motion_config2_reuse.csv", sc2, reuse=traces.reuse_flags(sc2))
+    sources = {"config2_reuse": (HERE / "motion_config2_reuse.csv", 8, "csv"),
+               "config5_high": (HERE / "motion_config5_high.csv", 16, "derived"),
+               "config3": (HERE / "motion_config3.csv", 50, "derived")}
+    cases = []
+    for pol in ("uniform", "recency", "motion", "reuse_weighted"):
+        for sa in (2162688, 4325376, 8650752):
+            for flags in ("csv", "none"):
+                cases.append(dict(trace="config2_reuse", policy=pol, set_aside=sa, flags=flags))
+        for pct in (10, 25, 50, 100):
+            cases.append(dict(trace="config5_high", policy=pol,
+                              set_aside=2 * MAX_PERSIST_B200 * pct // 100, flags="derived"))
+    for pol in ("recency", "reuse_weighted"):
+        cases.append(dict(trace="config3", policy=pol, set_aside=2 * MAX_PERSIST_B200,
+                          flags="derived"))
+    fixtures = []
+    for c in cases:
+        csv, frames, _ = sources[c["trace"]]
+        scores, col = O.read_motion_csv(csv, frames, 98, with_reuse=True)
+        reuse = {"csv": col, "derived": traces.reuse_flags(scores), "none": None}[c["flags"]]
+        got = R.run_reuse(scores, reuse, policy=c["policy"], frames=frames,
+                          set_aside=c["set_aside"])
+        mine = O.run_reuse(scores, reuse, policy=c["policy"], frames=frames,
+                           set_aside=c["set_aside"])
+        for key in ("copies", "restaged", "hits", "staged_bytes", "window_bytes", "maps"):
+            assert np.array_equal(got[key], mine[key]), (c, key)
+        per = [{"sha": digest(got["maps"][f]), "mapped": int((got["maps"][f] >= 0).sum()),
+                "copies": int(got["copies"][f]), "restaged": int(got["restaged"][f]),
+                "hits": int(got["hits"][f]), "staged_bytes": int(got["staged_bytes"][f]),
+                "window_bytes": int(got["window_bytes"][f])} for f in range(frames)]
+        fixtures.append({**c, "frames": frames, "elem_bytes": 4, "per_frame": per})
+        print("ok", c, flush=True)
+    (HERE / "kvmap_reuse_ref.json").write_text(json.dumps(
+        {"generator": "tests/golden/make_golden.py --only reuse", "tokens": T, "hidden": D,
+         "tile_tokens": TT, "reuse_rule": "traces/gen_motion_from_video.py:118-122, percentile 50",
+         "cases": fixtures}, indent=1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", choices=("reuse",), default=None,
+                    help="regenerate one fixture set only")
     args = ap.parse_args()
     ref = Path(args.ref)
     orc.build(str(ref))
+    if args.only == "reuse":
+        reuse_fixtures()
+        return
     from kvp import traces
 
     # ---- motion traces -------------------------------------------------
@@ -190,6 +248,7 @@ def main():
         "seed": tm["seed"], "frames": tm["frames"], "tiles": tm["tiles"],
         "validation_cosine_first_vs_last": tm["validation_cosine_first_vs_last"],
         "golden_per_frame_stats": gm["per_frame_stats"]}, indent=1))
+    reuse_fixtures()
     print("fixtures written to", HERE)
 
 
