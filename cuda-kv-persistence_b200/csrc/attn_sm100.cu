@@ -118,43 +118,7 @@ struct Params {
 };
 
 // ------------------------------------------------------------- primitives
-// (the shared ones are in sm100_ptx.h)
-// Bounded wait.  Returns false (and raises the CTA abort flag and the global
-// status) when the phase did not complete within kWaitNs, or when another
-// role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, Smem& sm, int* status) {
-    if (mbar_try_wait(b, parity)) return true;
-    const unsigned long long t0 = globaltimer();
-    for (;;) {
-        if (mbar_try_wait_sleep(b, parity)) return true;
-        if (*(volatile int*)&sm.abort_flag) return false;
-        if (globaltimer() - t0 > kWaitNs) {
-            *(volatile int*)&sm.abort_flag = 1;
-            atomicOr(status, KVP_STATUS_TIMEOUT);
-            return false;
-        }
-    }
-}
-// Warp-uniform bounded wait: every lane polls and the verdicts are combined
-// (a completed phase stays completed until this warp itself moves the
-// protocol on), so the warp stays converged for the .sync.aligned tcgen05
-// and shuffle instructions that follow.
-__device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t parity, Smem& sm, int* status) {
-    if (__any_sync(0xffffffffu, mbar_try_wait(b, parity))) return true;
-    const unsigned long long t0 = globaltimer();
-    for (;;) {
-        if (__any_sync(0xffffffffu, mbar_try_wait_sleep(b, parity))) return true;
-        if (__any_sync(0xffffffffu, *(volatile int*)&sm.abort_flag != 0)) return false;
-        if (__any_sync(0xffffffffu, globaltimer() - t0 > kWaitNs)) {
-            if ((threadIdx.x & 31) == 0) {
-                *(volatile int*)&sm.abort_flag = 1;
-                atomicOr(status, KVP_STATUS_TIMEOUT);
-            }
-            __syncwarp();
-            return false;
-        }
-    }
-}
+// (mbarriers, TMA, tcgen05, bounded waits: sm100_ptx.h)
 // One 128x128x128 GEMM as eight back-to-back K16 MMAs, issued in two asm
 // blocks (steps 0-5, then 6-7) so the issuer can test the next GEMM's
 // barriers while the first six are queued.  The descriptors of steps 1..7
@@ -1138,6 +1102,11 @@ int encode_map(CUtensorMap* m, const void* base, long long rows, long long cols,
 }
 
 }  // namespace
+
+int make_bf16_tensor_map(CUtensorMap* m, const void* base, long long rows, long long cols,
+                         long long pitch, uint32_t box_rows) {
+    return make_map(m, base, rows, cols, pitch, box_rows);
+}
 
 int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
                      bool allow_split) {

@@ -2,14 +2,12 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
-namespace kvp {
+#include "kvp_common.h"
 
-// Bits of the device status word (kvp_read_status).
-constexpr int KVP_STATUS_MAP = 1;      // a KVMap entry pointed outside the arena (base row read)
-constexpr int KVP_STATUS_TIMEOUT = 2;  // a bounded wait expired; the CTA's output is incomplete
-constexpr int KVP_STATUS_ALIGN = 4;    // dynamic shared memory not 1024-byte aligned; nothing computed
+namespace kvp {
 
 // One layer's buffers.  Q/K/V/Out are bf16 [rows][D] (head h at columns
 // [h*128, h*128+128)); the arena is bf16 [arena_rows][2*D] (K half, V half);
@@ -52,6 +50,12 @@ struct AttnDesc {
 // (callers that may not allocate) always runs one CTA per pair.
 int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
                      bool allow_split = true);
+
+// 2D TMA map of a bf16 row-major tensor [rows][cols] (row pitch `pitch`
+// elements), box 64 columns x box_rows rows, 128B swizzle.  Encoded maps are
+// cached by (base, shape, pitch, box).
+int make_bf16_tensor_map(CUtensorMap* m, const void* base, long long rows, long long cols,
+                         long long pitch, uint32_t box_rows);
 
 // A kernel whose bounded mbarrier wait cannot complete: records
 // KVP_STATUS_TIMEOUT after limit_ns (<= 5 s).  For tests of the timeout path.

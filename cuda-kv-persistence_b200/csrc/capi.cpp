@@ -10,6 +10,7 @@
 #include "kernels.h"
 #include "kv_tile_manager.h"
 #include "kvp_common.h"
+#include "qkv_sm100.h"
 #include "session.h"
 #include "tile_gating_policy.h"
 #include "tile_layout.h"
@@ -18,6 +19,7 @@ namespace kvp {
 
 namespace {
 thread_local char g_err[512] = "";
+}  // namespace
 
 // One device status word per device, allocated on first use.
 int* status_word() {
@@ -34,7 +36,6 @@ int* status_word() {
     }
     return words[dev];
 }
-}  // namespace
 
 void set_error(const char* fmt, ...) {
     va_list ap;
@@ -408,8 +409,48 @@ KVP_API int kvp_session_step(void* s, int frame, const float* scores_flat,
                                                 k_layers, v_layers, window_layer,
                                                 (cudaStream_t)stream);
 }
+KVP_API int kvp_session_stage_except(void* s, const void* const* k_layers,
+                                     const void* const* v_layers, long long skip_row0,
+                                     long long skip_rows, void* stream) {
+    return static_cast<kvp::Session*>(s)->stage(k_layers, v_layers, (cudaStream_t)stream, skip_row0,
+                                                skip_rows);
+}
+KVP_API int kvp_session_produce(void* s, int layer, const void* x, const void* w, const float* bias,
+                                void* q, void* k, void* v, long long row0, long long rows,
+                                void* stream) {
+    return static_cast<kvp::Session*>(s)->produce(layer, x, w, bias, q, k, v, row0, rows,
+                                                  (cudaStream_t)stream);
+}
 KVP_API int kvp_session_clear_window(void* s, void* stream) {
     return static_cast<kvp::Session*>(s)->clear_window((cudaStream_t)stream);
+}
+
+// ------------------------------------------------ QKV producer, LayerNorm
+struct kvp_qkv_io {
+    const void* x;
+    const void* w;
+    const float* bias;
+    void* q;
+    void* k;
+    void* v;
+    void* arena;
+    const long long* kvmap;
+    long long rows, map_row0, arena_rows;
+    int D;
+};
+
+KVP_API int kvp_qkv_project_bf16(const kvp_qkv_io* io, void* stream) {
+    if (!io) return kvp::KVP_ERR_ARG;
+    int* st = kvp::status_word();
+    if (!st) return kvp::KVP_ERR_CUDA;
+    kvp::QkvIO q{io->x, io->w, io->bias, io->q, io->k, io->v, io->arena, io->kvmap,
+                 io->rows, io->map_row0, io->arena_rows, io->D};
+    return kvp::launch_qkv_project_bf16(q, st, (cudaStream_t)stream);
+}
+
+KVP_API int kvp_layernorm_bf16(const void* x, const float* gamma, const float* beta, void* y,
+                               long long rows, int D, float eps, void* stream) {
+    return kvp::launch_layernorm_bf16(x, gamma, beta, y, rows, D, eps, (cudaStream_t)stream);
 }
 
 // --------------------------------------------------------- bf16 attention

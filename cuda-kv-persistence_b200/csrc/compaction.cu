@@ -38,10 +38,13 @@ __global__ void __launch_bounds__(256) copy_batch_kernel(const CopyOp* __restric
 }
 
 // One warp per (pair, layer): the K row then the V row of a source token
-// land in one arena row [K | V].  row_bytes must be a multiple of 16.
+// land in one arena row [K | V].  row_bytes must be a multiple of 16.  Pairs
+// whose source row lies in [skip_lo, skip_hi) are left alone (their arena
+// rows were written by the producer of those rows).
 __global__ void __launch_bounds__(256) gather_rows_kernel(GatherLayers L, int layers,
                                                           const int2* __restrict__ pairs, int n,
-                                                          int64_t row_bytes) {
+                                                          int64_t row_bytes, int64_t skip_lo,
+                                                          int64_t skip_hi) {
     const int warps_per_cta = blockDim.x >> 5;
     const int lane = threadIdx.x & 31;
     const int64_t total = (int64_t)n * layers;
@@ -50,6 +53,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherLayers L, int la
          w += (int64_t)gridDim.x * warps_per_cta) {
         const int layer = (int)(w / n);
         const int2 pr = pairs[w - (int64_t)layer * n];
+        if (pr.x >= skip_lo && pr.x < skip_hi) continue;
         const uint4* ks = reinterpret_cast<const uint4*>(
             static_cast<const char*>(L.k[layer]) + (int64_t)pr.x * row_bytes);
         const uint4* vs = reinterpret_cast<const uint4*>(
@@ -89,7 +93,7 @@ int launch_copy_batch(const CopyOp* d_ops, int n, cudaStream_t stream) {
 }
 
 int launch_gather_rows(const GatherLayers& L, int layers, const int32_t* d_pairs, int n,
-                       int64_t row_bytes, cudaStream_t stream) {
+                       int64_t row_bytes, cudaStream_t stream, int64_t skip_lo, int64_t skip_hi) {
     if (n <= 0 || layers <= 0) return KVP_OK;
     if (layers > kMaxLayers || (row_bytes & 15) != 0 || !d_pairs) {
         set_error("gather_rows: layers=%d (max %d), row_bytes=%lld must be a multiple of 16",
@@ -101,7 +105,7 @@ int launch_gather_rows(const GatherLayers& L, int layers, const int32_t* d_pairs
     const int64_t cap = (int64_t)sm_count() * 8;
     if (grid > cap) grid = cap;
     gather_rows_kernel<<<(unsigned)grid, 256, 0, stream>>>(
-        L, layers, reinterpret_cast<const int2*>(d_pairs), n, row_bytes);
+        L, layers, reinterpret_cast<const int2*>(d_pairs), n, row_bytes, skip_lo, skip_hi);
     KVP_CUDA(cudaGetLastError());
     return KVP_OK;
 }

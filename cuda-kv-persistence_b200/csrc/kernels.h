@@ -23,10 +23,12 @@ struct GatherLayers {
     void* arena[kMaxLayers];
 };
 
-// For i < n and every layer: arena[slot[i]] = K[row[i]] || V[row[i]].
-// pairs is a device int32 array [n][2] = (source row, arena slot).
+// For i < n and every layer: arena[slot[i]] = K[row[i]] || V[row[i]],
+// except rows in [skip_lo, skip_hi).  pairs is a device int32 array [n][2]
+// = (source row, arena slot).
 int launch_gather_rows(const GatherLayers& L, int layers, const int32_t* d_pairs, int n,
-                       int64_t row_bytes, cudaStream_t stream);
+                       int64_t row_bytes, cudaStream_t stream, int64_t skip_lo = 0,
+                       int64_t skip_hi = 0);
 
 // ---- FP32 remapped attention (csrc/attn_fp32.cu) --------------------------
 

@@ -21,11 +21,21 @@ enum Status : int {
     KVP_ERR_MAP = -6,        // a KVMap entry pointed outside the arena
 };
 
+// Bits of the device status word (kvp_read_status), set by the kernels.
+constexpr int KVP_STATUS_MAP = 1;      // a KVMap entry pointed outside the arena (base row used)
+constexpr int KVP_STATUS_TIMEOUT = 2;  // a bounded wait expired; the CTA's output is incomplete
+constexpr int KVP_STATUS_ALIGN = 4;    // dynamic shared memory not 1024-byte aligned; nothing computed
+
+// The current device's status word (device int, allocated on first use;
+// kvp_read_status reads and clears it).  nullptr if it cannot be allocated.
+int* status_word();
+
 // Records the message of the last failure on this thread.
 void set_error(const char* fmt, ...);
 const char* last_error();
 
-// Returns KVP_ERR_CUDA and records the message when e != cudaSuccess.
+// Records the message of CUDA error e and returns KVP_ERR_CUDA (call it
+// only for e != cudaSuccess; KVP_CUDA below does the check).
 int cuda_status(cudaError_t e, const char* what);
 
 // Per-device one-time setup (kernel attributes, launch checks): `run` is

@@ -6,6 +6,7 @@
 #include <cstring>
 
 #include "kvp_common.h"
+#include "qkv_sm100.h"
 
 namespace kvp {
 
@@ -349,16 +350,50 @@ int Session::upload(cudaStream_t s) {
     return KVP_OK;
 }
 
-int Session::stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s) {
-    if (!d_arena_ || !k_layers || !v_layers) return pairs_.empty() ? KVP_OK : KVP_ERR_ARG;
-    if (pairs_.empty()) return KVP_OK;
+int Session::stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s,
+                   int64_t skip_row0, int64_t skip_rows) {
+    const int64_t lo = skip_row0, hi = skip_row0 + (skip_rows > 0 ? skip_rows : 0);
+    bool any = false;
+    for (size_t i = 0; i < pairs_.size() && !any; i += 2) any = pairs_[i] < lo || pairs_[i] >= hi;
+    if (!any) return KVP_OK;   // nothing to copy (or every row was produced in place)
+    if (!d_arena_ || !k_layers || !v_layers) return KVP_ERR_ARG;
     GatherLayers L{};
     for (int l = 0; l < c_.layers; ++l) {
         L.k[l] = k_layers[l];
         L.v[l] = v_layers[l];
         L.arena[l] = arena(l);
     }
-    return launch_gather_rows(L, c_.layers, d_pairs_, (int)(pairs_.size() / 2), row_kv_bytes_, s);
+    return launch_gather_rows(L, c_.layers, d_pairs_, (int)(pairs_.size() / 2), row_kv_bytes_, s,
+                              lo, hi);
+}
+
+int Session::produce(int layer, const void* x, const void* w, const float* bias, void* q, void* k,
+                     void* v, int64_t row0, int64_t rows, cudaStream_t s) {
+    void* a = arena(layer);
+    if (c_.mode == MODE_REUSE || c_.elem_bytes != 2 || !d_map_ || rows <= 0 ||
+        row0 < info_.map_row0 || row0 + rows > info_.map_row0 + info_.map_rows) {
+        set_error("session produce: needs a bf16 session with device buffers, a mode other than "
+                  "reuse, and rows inside this step's map slice [%lld, %lld)",
+                  (long long)info_.map_row0, (long long)(info_.map_row0 + info_.map_rows));
+        return KVP_ERR_ARG;
+    }
+    int* st = status_word();
+    if (!st) return KVP_ERR_CUDA;
+    QkvIO io{};
+    io.x = x;
+    io.w = w;
+    io.bias = bias;
+    io.q = q;
+    io.k = k;
+    io.v = v;
+    const bool persist = c_.policy != POLICY_NONE && a;
+    io.arena = persist ? a : nullptr;
+    io.kvmap = persist ? reinterpret_cast<const long long*>(d_map_) : nullptr;
+    io.rows = rows;
+    io.map_row0 = row0;
+    io.arena_rows = cap_rows_;
+    io.D = c_.hidden;
+    return launch_qkv_project_bf16(io, st, s);
 }
 
 int Session::stage_layer(int layer, const void* k, const void* v, cudaStream_t s) {

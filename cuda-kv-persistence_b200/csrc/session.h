@@ -93,8 +93,19 @@ public:
     int64_t arena_layer_bytes() const { return arena_layer_bytes_; }
     // Uploads this step's map slice and copy list (pinned staging, async).
     int upload(cudaStream_t s);
-    // Gathers this step's rows into every layer's arena.
-    int stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s);
+    // Gathers this step's rows into every layer's arena, except source rows
+    // in [skip_row0, skip_row0 + skip_rows) (rows a produce() call wrote).
+    int stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s,
+              int64_t skip_row0 = 0, int64_t skip_rows = 0);
+    // Layer `layer`'s QKV projection of rows [row0, row0 + rows) (x bf16
+    // [rows][D], w bf16 [3D][D], bias fp32 [3D] or null) into q/k/v (bf16
+    // [rows][D], row 0 = row0; q may be null), writing every row this step
+    // maps into that layer's arena as well -- so stage() can skip them.
+    // Needs upload() of this step first, and a step in which every mapped
+    // row in the range is a copy (any mode but reuse, whose sticky hits keep
+    // their old slot contents); the range must lie in the step's map slice.
+    int produce(int layer, const void* x, const void* w, const float* bias, void* q, void* k,
+                void* v, int64_t row0, int64_t rows, cudaStream_t s);
     // Same for one layer (used when layers' K/V arrive one at a time).
     int stage_layer(int layer, const void* k, const void* v, cudaStream_t s);
     // Persisting window over layer's arena span (or a normal-property

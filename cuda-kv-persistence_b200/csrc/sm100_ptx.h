@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include "kvp_common.h"
+
 namespace kvp {
 namespace ptx {
 
@@ -168,6 +170,46 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+
+// Bounded wait (S: the kernel's shared-memory struct, with an int
+// abort_flag).  Returns false (and raises the CTA abort flag and the global
+// status) when the phase did not complete within kWaitNs, or when another
+// role already aborted.
+template <class S>
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, S& sm, int* status) {
+    if (mbar_try_wait(b, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+        if (mbar_try_wait_sleep(b, parity)) return true;
+        if (*(volatile int*)&sm.abort_flag) return false;
+        if (globaltimer() - t0 > kWaitNs) {
+            *(volatile int*)&sm.abort_flag = 1;
+            atomicOr(status, KVP_STATUS_TIMEOUT);
+            return false;
+        }
+    }
+}
+// Warp-uniform bounded wait: every lane polls and the verdicts are combined
+// (a completed phase stays completed until this warp itself moves the
+// protocol on), so the warp stays converged for the .sync.aligned tcgen05
+// and shuffle instructions that follow.
+template <class S>
+__device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t parity, S& sm, int* status) {
+    if (__any_sync(0xffffffffu, mbar_try_wait(b, parity))) return true;
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+        if (__any_sync(0xffffffffu, mbar_try_wait_sleep(b, parity))) return true;
+        if (__any_sync(0xffffffffu, *(volatile int*)&sm.abort_flag != 0)) return false;
+        if (__any_sync(0xffffffffu, globaltimer() - t0 > kWaitNs)) {
+            if ((threadIdx.x & 31) == 0) {
+                *(volatile int*)&sm.abort_flag = 1;
+                atomicOr(status, KVP_STATUS_TIMEOUT);
+            }
+            __syncwarp();
+            return false;
+        }
+    }
+}
 
 }  // namespace ptx
 }  // namespace kvp

@@ -45,6 +45,13 @@ class SessionConfig(C.Structure):
                 ("layers", C.c_int), ("set_aside", C.c_longlong)]
 
 
+class QkvIO(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("w", C.c_void_p), ("bias", C.c_void_p), ("q", C.c_void_p),
+                ("k", C.c_void_p), ("v", C.c_void_p), ("arena", C.c_void_p), ("kvmap", C.c_void_p),
+                ("rows", C.c_longlong), ("map_row0", C.c_longlong), ("arena_rows", C.c_longlong),
+                ("D", C.c_int)]
+
+
 class StepInfo(C.Structure):
     _fields_ = [("frame", C.c_int), ("sel_count", C.c_int), ("staged_tiles", C.c_int),
                 ("copies", C.c_int), ("map_row0", C.c_longlong), ("map_rows", C.c_longlong),
@@ -119,6 +126,14 @@ SIGNATURES = {
     "kvp_session_plan_frame_reuse": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "kvp_session_step": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.c_void_p, C.c_int, C.c_void_p]),
+    "kvp_session_stage_except": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong,
+                                           C.c_longlong, C.c_void_p]),
+    "kvp_session_produce": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong,
+                                      C.c_longlong, C.c_void_p]),
+    "kvp_qkv_project_bf16": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "kvp_layernorm_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong,
+                                     C.c_int, C.c_float, C.c_void_p]),
     "kvp_session_plan_stack": (C.c_int, [C.c_void_p, C.c_void_p]),
     "kvp_session_finish": (C.c_int, [C.c_void_p]),
     "kvp_session_info": (C.c_int, [C.c_void_p, C.POINTER(StepInfo)]),

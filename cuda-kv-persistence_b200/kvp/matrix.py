@@ -382,3 +382,102 @@ def run_reuse_matrix(*, reps: int = 3, frames: int = 16, tokens: int = 1560, hea
                         "tflops": round(flops / (t.mean() / 1e3) / 1e12, 2), "reps": len(t),
                         "device_status": status})
     return res
+
+
+
+def run_producer(*, reps: int = 20, warmup: int = 3, frames: int = 21, tokens: int = 1560,
+                 heads: int = 12, seed: int = 0, set_aside: int | None = None,
+                 device="cuda") -> list[dict]:
+    """One layer's K/V production for BASELINE config 4 (21 frames x 1560
+    tokens, D = 1536, stack admission by ReuseWeighted at the device's max
+    persisting L2), CUDA events over `reps` calls each:
+      fused         LayerNorm + the tcgen05 producer, which writes every
+                    admitted row into the arena in its epilogue (no gather)
+      unfused       LayerNorm + three cuBLAS GEMMs on the Q/K/V weight blocks
+                    (torch.mm into contiguous q/k/v, bias added) + the
+                    session's gather of the admitted rows
+      gemm_ours     the producer alone, no map
+      gemm_cublas   cuBLAS on the same [rows, 3D] product (torch.addmm)
+    x (100 MB) and the outputs (300 MB) exceed L2; W (14 MB) stays in it.
+    Arena equality of the fused and gather paths is checked by the GPU tests
+    (tests/test_gpu_producer.py)."""
+    from ._lib import DeviceInfo, lib
+    from .producer import layernorm, qkv_project
+    from .traces import motion_config4
+    import ctypes as C
+    if set_aside is None:
+        info = DeviceInfo()
+        lib().kvp_query_device(-1, C.byref(info))
+        set_aside = int(info.max_persisting_l2_bytes)
+    D = heads * 128
+    rows = frames * tokens
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(rows, D, generator=g).to(torch.bfloat16).to(device)
+    w = (0.02 * torch.randn(3 * D, D, generator=g)).to(torch.bfloat16).to(device)
+    b = (0.1 * torch.randn(3 * D, generator=g)).to(device)
+    gamma = (1 + 0.1 * torch.randn(D, generator=g)).to(device)
+    beta = (0.1 * torch.randn(D, generator=g)).to(device)
+    h = torch.empty_like(x)
+    q, k, v = (torch.empty(rows, D, dtype=torch.bfloat16, device=device) for _ in range(3))
+    y3 = torch.empty(rows, 3 * D, dtype=torch.bfloat16, device=device)
+    wq, wk, wv = (w[i * D:(i + 1) * D] for i in range(3))
+    b16 = b.to(torch.bfloat16)
+    bq, bk, bv = (b16[i * D:(i + 1) * D] for i in range(3))
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    scores = motion_config4(frames=frames, seed=seed, tiles=(tokens + 15) // 16)
+    s = Session(mode="stack", policy="reuse_weighted", frames=frames, tokens=tokens, hidden=D,
+                elem_bytes=2, set_aside=set_aside, layers=1)
+    try:
+        st = s.plan_stack(scores)
+        s.upload(stream)
+
+        def fused():
+            layernorm(x, gamma, beta, h, stream=stream)
+            s.produce(0, h, w, b, q, k, v, row0=0, stream=stream)
+
+        def unfused():
+            layernorm(x, gamma, beta, h, stream=stream)
+            torch.mm(h, wq.t(), out=q)
+            q.add_(bq)
+            torch.mm(h, wk.t(), out=k)
+            k.add_(bk)
+            torch.mm(h, wv.t(), out=v)
+            v.add_(bv)
+            s.stage([k.data_ptr()], [v.data_ptr()], stream)
+
+        def gemm_ours():
+            qkv_project(h, w, b, q, k, v, stream=stream)
+
+        def gemm_cublas():
+            torch.addmm(b16, h, w.t(), out=y3)
+
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+
+        def timed(fn):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / reps
+
+        read_status()
+        flop = 2.0 * rows * 3 * D * D
+        res = []
+        for name, fn in (("fused", fused), ("unfused", unfused), ("gemm_ours", gemm_ours),
+                         ("gemm_cublas", gemm_cublas)):
+            ms = timed(fn)
+            res.append({"leg": name, "ms": round(ms, 4),
+                        "gemm_tflops": round(flop / (ms / 1e3) / 1e12, 1), "rows": rows, "D": D,
+                        "admitted_rows": st.copies, "reps": reps})
+        status = read_status()
+        for r in res:
+            r["device_status"] = status
+        return res
+    finally:
+        torch.cuda.synchronize()
+        s.close()

@@ -144,6 +144,23 @@ class Session:
                                        None if r is None else r.ctypes.data, ka, va, window_layer,
                                        C.c_void_p(stream)), "step")
 
+    def stage_except(self, k_ptrs, v_ptrs, skip_row0: int, skip_rows: int, stream: int = 0):
+        """stage() without the source rows [skip_row0, skip_row0 + skip_rows)."""
+        n = len(k_ptrs)
+        ka = (C.c_void_p * max(n, 1))(*k_ptrs)
+        va = (C.c_void_p * max(n, 1))(*v_ptrs)
+        check(self._L.kvp_session_stage_except(self.h, ka, va, skip_row0, skip_rows,
+                                               C.c_void_p(stream)), "stage_except")
+
+    def produce(self, layer: int, x, w, bias, q, k, v, *, row0: int, stream: int = 0):
+        """Layer `layer`'s QKV projection of rows [row0, row0 + len(x)) with
+        this step's KVMap: mapped rows land in the arena in the epilogue
+        (call upload() first; skip these rows in stage_except)."""
+        def p(t):
+            return None if t is None else C.c_void_p(t.data_ptr())
+        check(self._L.kvp_session_produce(self.h, layer, p(x), p(w), p(bias), p(q), p(k), p(v),
+                                          row0, x.shape[0], C.c_void_p(stream)), "produce")
+
     def window(self, layer: int, stream: int = 0):
         check(self._L.kvp_session_window(self.h, layer, C.c_void_p(stream)), "window")
 

@@ -114,6 +114,35 @@ int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
 int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d,
                           const long long* host_kvmap, int* host_status, void* stream);
 
+/* ---- QKV producer: the block's LayerNorm and qkv_proj
+ * (src/backbone.py:13-33; nn.Linear(D, 3D) + view(b, t, 3, heads, head_dim))
+ * in bf16 with fp32 accumulation, tcgen05 GEMM.  x bf16 [rows][D] (rows >=
+ * 128, D a multiple of 256), w bf16 [3D][D] (Q rows, then K, then V), bias
+ * fp32 [3D] or NULL; Q/K/V bf16 [rows][D] (q may be NULL), head h at columns
+ * [128h, 128h+128).  When kvmap != NULL, row r's K and V are also written to
+ * arena row kvmap[map_row0 + r] (bf16 [arena_rows][2D], K half then V half)
+ * when that entry is in [0, arena_rows); entries >= arena_rows set status
+ * bit 0 and are skipped.  No reference counterpart: the reference computes
+ * K/V in PyTorch and never hands them to the CUDA path
+ * (src/backbone.py:16-22, 246-255).  All buffers 16-byte aligned. */
+typedef struct {
+    const void* x;
+    const void* w;
+    const float* bias;
+    void* q;
+    void* k;
+    void* v;
+    void* arena;
+    const long long* kvmap;
+    long long rows, map_row0, arena_rows;
+    int D;
+} kvp_qkv_io;
+int kvp_qkv_project_bf16(const kvp_qkv_io* io, void* stream);
+/* y = (x - mean) / sqrt(var + eps) * gamma + beta per row (nn.LayerNorm,
+ * biased variance): x, y bf16 [rows][D] (D % 8 == 0), gamma/beta fp32 [D]. */
+int kvp_layernorm_bf16(const void* x, const float* gamma, const float* beta, void* y,
+                       long long rows, int D, float eps, void* stream);
+
 /* ---- Session: the per-frame admission loop / KVMap emitter of
  * src/run_policy_experiment.cu:156-274 as a library. */
 typedef struct {
@@ -163,6 +192,17 @@ int kvp_session_stage(void* s, const void* const* k_layers, const void* const* v
 int kvp_session_stage_layer(void* s, int layer, const void* k, const void* v, void* stream);
 int kvp_session_window(void* s, int layer, void* stream);
 int kvp_session_clear_window(void* s, void* stream);
+/* kvp_session_stage without the source rows [skip_row0, skip_row0 +
+ * skip_rows): the rows a kvp_session_produce call wrote in place. */
+int kvp_session_stage_except(void* s, const void* const* k_layers, const void* const* v_layers,
+                             long long skip_row0, long long skip_rows, void* stream);
+/* Layer `layer`'s kvp_qkv_project_bf16 of rows [row0, row0 + rows) with this
+ * step's device KVMap and that layer's arena (after kvp_session_upload): the
+ * rows it maps land in the arena with no gather.  bf16 sessions only; not
+ * in reuse mode (a sticky hit keeps its old slot contents); the rows must lie
+ * in this step's map slice (kvp_step_info map_row0 / map_rows). */
+int kvp_session_produce(void* s, int layer, const void* x, const void* w, const float* bias,
+                        void* q, void* k, void* v, long long row0, long long rows, void* stream);
 /* One per-frame step in one call (no reference counterpart; the reference
  * driver does these steps inline, src/run_policy_experiment.cu:156-274):
  * kvp_session_plan_frame_reuse (reuse_flat is read in reuse mode only),

@@ -1,6 +1,6 @@
 """Regenerates the committed golden fixtures from the reference's own code.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--only reuse]
+    python tests/golden/make_golden.py [--ref /root/reference] [--only reuse|qkv]
 
 Needs the reference sources (read, never copied) and is run once, on a host
 where they exist; the tests only read the files it writes:
@@ -30,6 +30,10 @@ where they exist; the tests only read the files it writes:
                           ``motion_config2_reuse.csv`` (a trace carrying the
                           optional reuse column).  ``--only reuse`` rewrites
                           just these two files.
+* ``qkv_ref.npz``         the reference's DiTSelfAttentionBlock (its
+                          LayerNorm, qkv_proj and view/permute) on seeded
+                          inputs (``oracle/qkv.py qkv_params``): sampled rows of h, Q, K, V
+                          and per-column sums.  ``--only qkv``.
 """
 
 from __future__ import annotations
@@ -143,16 +147,56 @@ def reuse_fixtures():
          "cases": fixtures}, indent=1))
 
 
+QKV_SEED, QKV_ROWS, QKV_D = 31, 160, 256
+QKV_SAMPLE_ROWS = [0, 1, 57, 127, 128, 159]
+
+
+def qkv_fixture(ref: Path):
+    """qkv_ref.npz: the reference's own DiTSelfAttentionBlock
+    (src/backbone.py:8-33), loaded with oracle.qkv.qkv_params(), run on one frame: its
+    LayerNorm output and the Q (qkv_proj(norm(x)) split by the module's own
+    view/permute) and the K, V its forward returns, for QKV_SAMPLE_ROWS
+    (full rows) plus every column's sum over all rows."""
+    import torch
+    sys.path.insert(0, str(ref))
+    from src.backbone import DiTSelfAttentionBlock
+    from src.config import BackboneConfig
+    cfg = BackboneConfig(num_layers=1, hidden_dim=QKV_D, num_heads=QKV_D // 128, head_dim=128,
+                         tokens_per_frame=QKV_ROWS, latent_grid_rows=10, latent_grid_cols=16)
+    blk = DiTSelfAttentionBlock(cfg).eval()
+    from oracle.qkv import qkv_params
+    x, gamma, beta, w, b = qkv_params(QKV_SEED, QKV_ROWS, QKV_D)
+    with torch.no_grad():
+        blk.norm.weight.copy_(torch.from_numpy(gamma))
+        blk.norm.bias.copy_(torch.from_numpy(beta))
+        blk.attn.qkv_proj.weight.copy_(torch.from_numpy(w))
+        blk.attn.qkv_proj.bias.copy_(torch.from_numpy(b))
+        xt = torch.from_numpy(x)[None]
+        h = blk.norm(xt)
+        _, k, v = blk(xt)                                   # [1, heads, t, hd]
+        qkv = blk.attn.qkv_proj(h).view(1, QKV_ROWS, 3, cfg.num_heads, cfg.head_dim)
+        q = qkv.permute(2, 0, 3, 1, 4).unbind(0)[0]
+    flat = lambda t: t[0].permute(1, 0, 2).reshape(QKV_ROWS, QKV_D).numpy()   # [t, heads*hd]
+    q, k, v, h = flat(q), flat(k), flat(v), h[0].numpy()
+    rows = np.array(QKV_SAMPLE_ROWS)
+    np.savez_compressed(HERE / "qkv_ref.npz", seed=QKV_SEED, rows=QKV_ROWS, D=QKV_D,
+                        sample_rows=rows, h=h[rows], q=q[rows], k=k[rows], v=v[rows],
+                        q_colsum=q.sum(0), k_colsum=k.sum(0), v_colsum=v.sum(0))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=("reuse",), default=None,
+    ap.add_argument("--only", choices=("reuse", "qkv"), default=None,
                     help="regenerate one fixture set only")
     args = ap.parse_args()
     ref = Path(args.ref)
     orc.build(str(ref))
     if args.only == "reuse":
         reuse_fixtures()
+        return
+    if args.only == "qkv":
+        qkv_fixture(ref)
         return
     from kvp import traces
 
@@ -249,6 +293,7 @@ def main():
         "validation_cosine_first_vs_last": tm["validation_cosine_first_vs_last"],
         "golden_per_frame_stats": gm["per_frame_stats"]}, indent=1))
     reuse_fixtures()
+    qkv_fixture(ref)
     print("fixtures written to", HERE)
 
 

@@ -105,3 +105,19 @@ def test_reference_trace_and_golden_statistics():
     for f, st in enumerate(meta["golden_per_frame_stats"]):
         assert round(float(out[f].mean()), 6) == st["mean"], f
         assert round(float(out[f].std()), 6) == st["std"], f
+
+
+def test_qkv_oracle_matches_reference_block():
+    """oracle/qkv.py (LayerNorm, qkv_proj, column split) against the
+    reference's DiTSelfAttentionBlock run on the same seeded inputs
+    (tests/golden/qkv_ref.npz, written by make_golden.py --only qkv)."""
+    from oracle.qkv import layernorm, qkv_params, qkv_split
+    g = np.load(GOLDEN / "qkv_ref.npz")
+    x, gamma, beta, w, b = qkv_params(int(g["seed"]), int(g["rows"]), int(g["D"]))
+    h = layernorm(x, gamma, beta)
+    q, k, v = qkv_split(h, w, b)
+    rows = g["sample_rows"]
+    np.testing.assert_allclose(h[rows], g["h"], rtol=0, atol=1e-5)
+    for name, got in (("q", q), ("k", k), ("v", v)):
+        np.testing.assert_allclose(got[rows], g[name], rtol=0, atol=1e-5, err_msg=name)
+        np.testing.assert_allclose(got.sum(0), g[f"{name}_colsum"], rtol=0, atol=1e-3, err_msg=name)
