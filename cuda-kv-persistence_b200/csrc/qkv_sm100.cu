@@ -13,23 +13,28 @@
 // gather launch, and attention through the arena stays bitwise equal to
 // attention over the base rows.
 //
-// GEMM: persistent CTAs (one per SM) walk the 128 x 256 output tiles in
+// GEMM: persistent CTAs (one per SM) walk the 256 x 256 output tiles in
 // row-major tile order (concurrent CTAs share A row blocks; all of W stays
-// in L2).  Per CTA (384 threads):
-//   warp 0      TMA producer: per 64-column K block one A box [128][64] and
-//               one B box [256][64], 128B swizzle, into a 4-stage ring
-//   warp 1      TMEM allocation (512 columns = two 256-column accumulators)
-//               and the single-thread MMA issuer: per K block four
-//               tcgen05.mma M128 N256 K16, then a commit that frees the ring
-//               stage; per tile a commit that hands the accumulator over
-//   warps 4-11  epilogue: warp w reads TMEM lanes 32*(w%4).. (its 32 rows)
-//               and columns [128*((w-4)/4), +128) of the tile, adds the bias,
-//               rounds to bf16 and stores 16-byte vectors to the Q/K/V rows
-//               and, for admitted rows, to the arena
-// The accumulators alternate, so a tile's epilogue overlaps the next tile's
-// MMAs.  Every mbarrier wait is bounded (about one second): on expiry the
-// CTA records KVP_STATUS_TIMEOUT, waits (bounded) for its own TMA loads and
-// MMAs in flight, frees TMEM and returns.
+// in L2).  A tile is two 128-row halves that share every B tile: per K block
+// an SM takes in 64 KB for 2 x 128 x 256 x 64 MACs, the rate one SM's L2
+// port sustains at the tensor pipe's pace (a 128 x 256 tile needs half as
+// many MACs per byte and stalls on L2 ingress at ~60% tensor use).  Per CTA
+// (384 threads):
+//   warp 0      TMA producer: per 64-column K block two A boxes [128][64]
+//               and one B box [256][64], 128B swizzle, into a 3-stage ring
+//   warp 1      TMEM allocation (all 512 columns: one 256-column accumulator
+//               per half) and the single-thread MMA issuer: per K block
+//               tcgen05.mma M128 N256 K16 x 4 for each half, then a commit
+//               that frees the ring stage; per tile a commit that hands the
+//               accumulators to the epilogue
+//   warps 4-11  epilogue: warp w reads TMEM lanes 32*(w%4).. of half
+//               (w-4)/4 (its 32 rows, all 256 columns), adds the bias, rounds
+//               to bf16 and stores 16-byte vectors to the Q/K/V rows and, for
+//               admitted rows, to the arena
+// TMEM holds one tile, so the next tile's MMAs wait for the epilogue (about a
+// tenth of a tile's MMA time).  Every mbarrier wait is bounded (about one
+// second): on expiry the CTA records KVP_STATUS_TIMEOUT, waits (bounded) for
+// its own TMA loads and MMAs in flight, frees TMEM and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -44,21 +49,24 @@ namespace {
 
 using namespace ptx;
 
-constexpr int kGM = 128;          // output rows per tile (TMEM lanes)
+constexpr int kGM = 256;          // output rows per tile (two 128-row halves)
+constexpr int kGH = 128;          // rows per half (TMEM lanes, MMA M)
 constexpr int kGN = 256;          // output columns per tile (MMA N)
 constexpr int kGK = 64;           // K block: one 128-byte swizzle row of bf16
-constexpr int kGStages = 4;       // depth of the A/B ring
+constexpr int kGStages = 3;       // depth of the A/B ring
 constexpr int kGThreads = 384;    // producer, MMA, 2 idle, 8 epilogue warps
-constexpr uint32_t kABytes = kGM * kGK * 2;   // 16 KB
-constexpr uint32_t kBBytes = kGN * kGK * 2;   // 32 KB
+constexpr uint32_t kHalfBytes = kGH * kGK * 2;  // 16 KB: one half's A box
+constexpr uint32_t kABytes = kGM * kGK * 2;     // 32 KB
+constexpr uint32_t kBBytes = kGN * kGK * 2;     // 32 KB
 
 struct __align__(1024) GSmem {
     uint8_t a[kGStages][kABytes];
     uint8_t b[kGStages][kBBytes];
+    uint8_t stage_out[8][32 * 128];  // per epilogue warp: 32 rows x 64 bf16
     uint64_t full[kGStages];      // TMA bytes of the stage landed
     uint64_t empty[kGStages];     // the stage's MMAs completed
-    uint64_t acc_full[2];         // the tile's last MMA completed
-    uint64_t acc_empty[2];        // the epilogue read the accumulator (8 warps)
+    uint64_t acc_full;            // the tile's last MMA completed
+    uint64_t acc_empty;           // the epilogue read the accumulators (8 warps)
     uint64_t mma_done;            // every MMA this CTA issued completed
     uint32_t tmem_base;
     int abort_flag;
@@ -82,7 +90,7 @@ struct GParams {
 // kind::f16 instruction descriptor: bf16 x bf16 -> f32, A and B K-major,
 // M = 128, N = 256.
 constexpr uint32_t kIdescM128N256 = (1u << 4) | (1u << 7) | (1u << 10) |
-                                    ((uint32_t)(kGN >> 3) << 17) | ((uint32_t)(kGM >> 4) << 24);
+                                    ((uint32_t)(kGN >> 3) << 17) | ((uint32_t)(kGH >> 4) << 24);
 
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
@@ -103,10 +111,8 @@ qkv_proj_sm100_kernel(const __grid_constant__ CUtensorMap map_x,
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(&sm.acc_full[a], 1);
-            mbar_init(&sm.acc_empty[a], 8);
-        }
+        mbar_init(&sm.acc_full, 1);
+        mbar_init(&sm.acc_empty, 8);
         mbar_init(&sm.mma_done, 1);
         sm.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -135,7 +141,10 @@ qkv_proj_sm100_kernel(const __grid_constant__ CUtensorMap map_x,
                 for (int kb = 0; kb < P.kblocks; ++kb) {
                     if (!(ok = mbar_wait(&sm.empty[stage], phase ^ 1u, sm, P.status))) break;
                     mbar_arrive_expect_tx(&sm.full[stage], P.stage_bytes);
+                    // (the second half's box may start past the last row: it
+                    // reads zeros, and its bytes still count)
                     tma_load_2d(sm.a[stage], &map_x, kb * kGK, m0, &sm.full[stage]);
+                    tma_load_2d(sm.a[stage] + kHalfBytes, &map_x, kb * kGK, m0 + kGH, &sm.full[stage]);
                     tma_load_2d(sm.b[stage], &map_w, kb * kGK, n0, &sm.full[stage]);
                     ++issued;
                     if (++stage == kGStages) { stage = 0; phase ^= 1u; }
@@ -161,24 +170,26 @@ qkv_proj_sm100_kernel(const __grid_constant__ CUtensorMap map_x,
             int i = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < P.n_tiles && ok; t += gridDim.x, ++i) {
-                const int acc = i & 1;
-                if (!(ok = mbar_wait(&sm.acc_empty[acc], ((i >> 1) & 1) ^ 1u, sm, P.status))) break;
+                if (!(ok = mbar_wait(&sm.acc_empty, (i & 1) ^ 1u, sm, P.status))) break;
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)acc * kGN;
                 for (int kb = 0; kb < P.kblocks; ++kb) {
                     if (!(ok = mbar_wait(&sm.full[stage], phase, sm, P.status))) break;
                     tc_fence_after();
                     const uint64_t da = sw128_desc(smem_u32(sm.a[stage]), 16, 1024);
                     const uint64_t db = sw128_desc(smem_u32(sm.b[stage]), 16, 1024);
                     // K16 step ks starts 32 bytes further into the 128-byte
-                    // swizzle row: +2 in the descriptor's 16-byte address field.
+                    // swizzle row: +2 in the descriptor's 16-byte address
+                    // field; the second half's A box is 16 KB further (+1024).
 #pragma unroll
-                    for (int ks = 0; ks < kGK / 16; ++ks)
-                        tc_mma(d, da + 2 * ks, db + 2 * ks, kIdescM128N256, (kb | ks) != 0);
+                    for (int ks = 0; ks < kGK / 16; ++ks) {
+                        tc_mma(tmem, da + 2 * ks, db + 2 * ks, kIdescM128N256, (kb | ks) != 0);
+                        tc_mma(tmem + kGN, da + (kHalfBytes >> 4) + 2 * ks, db + 2 * ks,
+                               kIdescM128N256, (kb | ks) != 0);
+                    }
                     tc_commit(&sm.empty[stage]);
                     if (++stage == kGStages) { stage = 0; phase ^= 1u; }
                 }
-                if (ok) tc_commit(&sm.acc_full[acc]);
+                if (ok) tc_commit(&sm.acc_full);
             }
             // Every MMA issued has completed before TMEM is freed.
             tc_commit(&sm.mma_done);
@@ -188,66 +199,91 @@ qkv_proj_sm100_kernel(const __grid_constant__ CUtensorMap map_x,
         }
     } else if (warp >= 4) {
         // --------------------------------------------------------- epilogue
+        // Per 64-column pair: TMEM -> registers (thread = row), + bias, bf16,
+        // into this warp's staging rows; then read back so that one store
+        // instruction writes 4 rows x 128 contiguous bytes (full lines)
+        // instead of 32 rows x 16 bytes.  Staging row r keeps its eight
+        // 16-byte chunks at positions chunk ^ (r & 7): both the row-wise
+        // writes and the chunk-wise reads are free of bank conflicts.
         const int quarter = warp & 3;          // TMEM lanes 32*quarter ..
-        const int half = (warp - 4) >> 2;      // tile columns [128*half, +128)
+        const int half = (warp - 4) >> 2;      // tile rows [128*half, +128)
+        uint8_t* stg = sm.stage_out[warp - 4];
+        const int cc = lane & 7;               // store phase: 16-byte chunk of a row
+        const int rsub = lane >> 3;            // store phase: row 4*j + rsub
         const long long D = P.D;
         int i = 0;
         for (int t = blockIdx.x; t < P.n_tiles; t += gridDim.x, ++i) {
-            const int acc = i & 1;
-            if (!warp_wait(&sm.acc_full[acc], (i >> 1) & 1, sm, P.status)) break;
+            if (!warp_wait(&sm.acc_full, i & 1, sm, P.status)) break;
             tc_fence_after();
-            const long long row = (long long)(t / P.n_tiles_n) * kGM + quarter * 32 + lane;
+            const long long wrow0 = (long long)(t / P.n_tiles_n) * kGM + half * kGH + quarter * 32;
             const int n0 = (t % P.n_tiles_n) * kGN;
             const int region = n0 / P.D;                 // 0 Q, 1 K, 2 V (D % 256 == 0)
-            const int col0 = n0 - region * P.D + half * 128;
-            const bool valid = row < P.rows;
-            __nv_bfloat16* dst = region == 0 ? P.q : region == 1 ? P.k : P.v;
-            if (dst && valid) dst += row * D + col0;
-            else dst = nullptr;
-            __nv_bfloat16* adst = nullptr;
-            if (region > 0 && valid && P.kvmap && P.arena) {
-                const long long slot = P.kvmap[P.map_row0 + row];
-                if (slot >= P.arena_rows) atomicOr(P.status, KVP_STATUS_MAP);
-                else if (slot >= 0) adst = P.arena + slot * 2 * D + (region - 1) * D + col0;
+            const int col0 = n0 - region * P.D;
+            long long my_slot = -1;                      // arena slot of row wrow0 + lane
+            if (region > 0 && wrow0 + lane < P.rows && P.kvmap && P.arena) {
+                const long long sl = P.kvmap[P.map_row0 + wrow0 + lane];
+                if (sl >= P.arena_rows) atomicOr(P.status, KVP_STATUS_MAP);
+                else if (sl >= 0) my_slot = sl;
             }
-            const float* bias = P.bias ? P.bias + n0 + half * 128 : nullptr;
-            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kGN + half * 128);
+            long long slot_j[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) slot_j[j] = __shfl_sync(0xffffffffu, my_slot, 4 * j + rsub);
+            __nv_bfloat16* base = region == 0 ? P.q : region == 1 ? P.k : P.v;
+            __nv_bfloat16* arena = P.arena ? P.arena + (region - 1) * D + col0 : nullptr;
+            const float* bias = P.bias ? P.bias + n0 : nullptr;
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * kGN);
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[32];
-                KVP_TMEM_LD32(taddr + c * 32, r);
-                KVP_TMEM_WAIT_LD_DEP(r);
-                float bv[32];
-                if (bias) {
-                    const float4* b4 = reinterpret_cast<const float4*>(bias + c * 32);
+            for (int p = 0; p < kGN / 64; ++p) {
+#pragma unroll 1
+                for (int c2 = 0; c2 < 2; ++c2) {
+                    const int c = 2 * p + c2;
+                    uint32_t r[32];
+                    KVP_TMEM_LD32(taddr + c * 32, r);
+                    KVP_TMEM_WAIT_LD_DEP(r);
+                    float bv[32];
+                    if (bias) {
+                        const float4* b4 = reinterpret_cast<const float4*>(bias + c * 32);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 x = __ldg(b4 + j);
-                        bv[4 * j] = x.x; bv[4 * j + 1] = x.y; bv[4 * j + 2] = x.z; bv[4 * j + 3] = x.w;
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 x = __ldg(b4 + j);
+                            bv[4 * j] = x.x; bv[4 * j + 1] = x.y; bv[4 * j + 2] = x.z; bv[4 * j + 3] = x.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) bv[j] = 0.f;
                     }
-                } else {
+                    uint32_t pk[16];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) bv[j] = 0.f;
-                }
-                uint32_t pk[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    pk[j] = pack_bf16(__uint_as_float(r[2 * j]) + bv[2 * j],
-                                      __uint_as_float(r[2 * j + 1]) + bv[2 * j + 1]);
-                if (dst) {
+                    for (int j = 0; j < 16; ++j)
+                        pk[j] = pack_bf16(__uint_as_float(r[2 * j]) + bv[2 * j],
+                                          __uint_as_float(r[2 * j + 1]) + bv[2 * j + 1]);
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        st_global_v4(dst + c * 32 + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                        *reinterpret_cast<uint4*>(stg + lane * 128 + (((c2 * 4 + j) ^ (lane & 7)) << 4)) =
+                            make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
                 }
-                if (adst) {
+                if (p == kGN / 64 - 1) {
+                    // every TMEM column of the tile is in registers or staged:
+                    // the next tile's MMAs may start while the stores drain
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.acc_empty);
+                }
+                __syncwarp();
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        st_global_v4(adst + c * 32 + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                for (int j = 0; j < 8; ++j) {
+                    const int rr = 4 * j + rsub;
+                    const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((cc ^ (rr & 7)) << 4));
+                    const long long grow = wrow0 + rr;
+                    if (grow < P.rows) {
+                        const int col = p * 64 + cc * 8;
+                        if (base) st_global_v4(base + grow * D + col0 + col, val.x, val.y, val.z, val.w);
+                        if (slot_j[j] >= 0)
+                            st_global_v4(arena + slot_j[j] * 2 * D + col, val.x, val.y, val.z, val.w);
+                    }
                 }
+                __syncwarp();
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
         }
     }
     tc_fence_before();
@@ -326,7 +362,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 int launch_qkv_project_bf16(const QkvIO& io, int* d_status, cudaStream_t stream) {
     const long long D = io.D;
     const long long m_tiles = (io.rows + kGM - 1) / kGM;
-    if (!io.x || !io.w || !io.k || !io.v || io.rows < kGM || D < 256 || D % 256 != 0 ||
+    if (!io.x || !io.w || !io.k || !io.v || io.rows < kGH || D < 256 || D % 256 != 0 ||
         D > (1 << 16) || io.map_row0 < 0 || (io.kvmap && (!io.arena || io.arena_rows < 0)) ||
         !aligned16(io.x) || !aligned16(io.w) || !aligned16(io.k) || !aligned16(io.v) ||
         (io.q && !aligned16(io.q)) || (io.arena && !aligned16(io.arena)) ||
@@ -343,10 +379,10 @@ int launch_qkv_project_bf16(const QkvIO& io, int* d_status, cudaStream_t stream)
     });
     if (rc_setup != KVP_OK) return rc_setup;
 
-    // The last row block's box reaches past `rows`: TMA fills those rows with
-    // zeros (and counts their bytes), the epilogue stores no row >= rows.
+    // The last row block's boxes reach past `rows`: TMA fills those rows
+    // with zeros (and counts their bytes), the epilogue stores no row >= rows.
     CUtensorMap mx, mw;
-    int rc = make_bf16_tensor_map(&mx, io.x, io.rows, D, D, kGM);
+    int rc = make_bf16_tensor_map(&mx, io.x, io.rows, D, D, kGH);
     if (rc != KVP_OK) return rc;
     rc = make_bf16_tensor_map(&mw, io.w, 3 * D, D, D, kGN);
     if (rc != KVP_OK) return rc;
