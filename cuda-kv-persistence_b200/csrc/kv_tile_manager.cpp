@@ -218,10 +218,10 @@ bool KVTileManager::streaming_begin() {
 bool KVTileManager::streaming_reserve(long row_id, size_t bytes_kv, bool changed, long* out_slot,
                                       bool* copy_needed, bool* was_held) {
     // :153-192 -- a sticky hit costs nothing unless the row changed.
-    auto it = row_slot_.find(row_id);
-    if (was_held) *was_held = it != row_slot_.end();
-    if (it != row_slot_.end()) {
-        *out_slot = it->second;
+    const long* held = row_slot_.find(row_id);
+    if (was_held) *was_held = held != nullptr;
+    if (held) {
+        *out_slot = *held;
         if (!changed) { *copy_needed = false; return true; }
         staged_bytes_ += bytes_kv;
         *copy_needed = true;
@@ -230,7 +230,7 @@ bool KVTileManager::streaming_reserve(long row_id, size_t bytes_kv, bool changed
     if (free_slots_.empty()) return false;
     const long slot = free_slots_.back();
     free_slots_.pop_back();
-    row_slot_[row_id] = slot;
+    row_slot_.put(row_id, slot);
     staged_bytes_ += bytes_kv;
     if (slot > slot_high_water_) slot_high_water_ = slot;
     *out_slot = slot;
@@ -254,10 +254,10 @@ bool KVTileManager::streaming_stage(long row_id, const void* k_dev, size_t k_byt
 
 bool KVTileManager::streaming_release(long row_id) {
     // :194-200 -- the freed slot goes back on top of the stack.
-    auto it = row_slot_.find(row_id);
-    if (it == row_slot_.end()) return false;
-    free_slots_.push_back(it->second);
-    row_slot_.erase(it);
+    const long* held = row_slot_.find(row_id);
+    if (!held) return false;
+    free_slots_.push_back(*held);
+    row_slot_.erase(row_id);
     return true;
 }
 

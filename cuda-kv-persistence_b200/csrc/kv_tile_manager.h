@@ -19,6 +19,8 @@
 #include <cstddef>
 #include <cstdint>
 #include <unordered_map>
+
+#include "slot_map.h"
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -127,7 +129,7 @@ private:
     size_t arena_next_row_ = 0;
     size_t arena_used_ = 0;
 
-    std::unordered_map<long, long> row_slot_;
+    SlotMap row_slot_;
     std::vector<long> free_slots_;
     long slot_high_water_ = -1;
     size_t staged_bytes_ = 0;
