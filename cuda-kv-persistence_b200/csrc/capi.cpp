@@ -10,6 +10,7 @@
 #include "kernels.h"
 #include "kv_tile_manager.h"
 #include "kvp_common.h"
+#include "motion_sm100.h"
 #include "qkv_sm100.h"
 #include "session.h"
 #include "tile_gating_policy.h"
@@ -451,6 +452,44 @@ KVP_API int kvp_qkv_project_bf16(const kvp_qkv_io* io, void* stream) {
 KVP_API int kvp_layernorm_bf16(const void* x, const float* gamma, const float* beta, void* y,
                                long long rows, int D, float eps, void* stream) {
     return kvp::launch_layernorm_bf16(x, gamma, beta, y, rows, D, eps, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------- motion producer
+struct kvp_motion_params {
+    int height, width, levels, winsize, iterations, poly_n;
+    float poly_sigma, pyr_scale;
+    int grid_rows, grid_cols, tile_cells;
+};
+
+KVP_API void* kvp_motion_create(const kvp_motion_params* p) {
+    if (!p) return nullptr;
+    kvp::MotionParams q{p->height, p->width, p->levels, p->winsize, p->iterations, p->poly_n,
+                        p->poly_sigma, p->pyr_scale, p->grid_rows, p->grid_cols, p->tile_cells};
+    auto* m = new (std::nothrow) kvp::MotionProducer(q);
+    if (m && m->status() != kvp::KVP_OK) {
+        delete m;
+        return nullptr;
+    }
+    return m;
+}
+KVP_API void kvp_motion_destroy(void* m) { delete static_cast<kvp::MotionProducer*>(m); }
+KVP_API int kvp_motion_tiles(void* m) { return static_cast<kvp::MotionProducer*>(m)->tiles(); }
+KVP_API int kvp_motion_flow(void* m, const void* d_prev, const void* d_next, float* d_flow,
+                            void* stream) {
+    return static_cast<kvp::MotionProducer*>(m)->pair_flow(static_cast<const uint8_t*>(d_prev),
+                                                           static_cast<const uint8_t*>(d_next),
+                                                           d_flow, (cudaStream_t)stream);
+}
+KVP_API int kvp_motion_trace(void* m, const void* d_frames, int frames, float* d_change,
+                             void* stream) {
+    return static_cast<kvp::MotionProducer*>(m)->trace(static_cast<const uint8_t*>(d_frames), frames,
+                                                       d_change, (cudaStream_t)stream);
+}
+KVP_API int kvp_motion_threshold(const float* change, int frames, int tiles, double percentile,
+                                 signed char* reuse, signed char* is_static, double* tau) {
+    return kvp::motion_threshold(change, frames, tiles, percentile,
+                                 reinterpret_cast<int8_t*>(reuse),
+                                 reinterpret_cast<int8_t*>(is_static), tau);
 }
 
 // --------------------------------------------------------- bf16 attention

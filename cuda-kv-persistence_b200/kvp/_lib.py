@@ -52,6 +52,13 @@ class QkvIO(C.Structure):
                 ("D", C.c_int)]
 
 
+class MotionParams(C.Structure):
+    _fields_ = [("height", C.c_int), ("width", C.c_int), ("levels", C.c_int), ("winsize", C.c_int),
+                ("iterations", C.c_int), ("poly_n", C.c_int), ("poly_sigma", C.c_float),
+                ("pyr_scale", C.c_float), ("grid_rows", C.c_int), ("grid_cols", C.c_int),
+                ("tile_cells", C.c_int)]
+
+
 class StepInfo(C.Structure):
     _fields_ = [("frame", C.c_int), ("sel_count", C.c_int), ("staged_tiles", C.c_int),
                 ("copies", C.c_int), ("map_row0", C.c_longlong), ("map_rows", C.c_longlong),
@@ -132,6 +139,13 @@ SIGNATURES = {
                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong,
                                       C.c_longlong, C.c_void_p]),
     "kvp_qkv_project_bf16": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "kvp_motion_create": (C.c_void_p, [C.c_void_p]),
+    "kvp_motion_destroy": (None, [C.c_void_p]),
+    "kvp_motion_tiles": (C.c_int, [C.c_void_p]),
+    "kvp_motion_flow": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "kvp_motion_trace": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "kvp_motion_threshold": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_double, C.c_void_p,
+                                       C.c_void_p, C.c_void_p]),
     "kvp_layernorm_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_longlong,
                                      C.c_int, C.c_float, C.c_void_p]),
     "kvp_session_plan_stack": (C.c_int, [C.c_void_p, C.c_void_p]),

@@ -481,3 +481,48 @@ def run_producer(*, reps: int = 20, warmup: int = 3, frames: int = 21, tokens: i
     finally:
         torch.cuda.synchronize()
         s.close()
+
+
+def run_motion(*, frames: int = 20, reps: int = 5, seed: int = 0, cpu_pairs: int = 4,
+               device="cuda") -> list[dict]:
+    """The motion-trace producer on a seeded 480 x 832 clip: GPU change rates
+    for all frame pairs (CUDA events over `reps` passes), and the
+    reference's own flow call (OpenCV Farneback on the host cores, the
+    threads OpenCV uses) timed on `cpu_pairs` pairs of the same clip."""
+    import time
+    from .motion import MotionProducer
+    from .traces import synthetic_video
+    clip = synthetic_video(frames, seed=seed)
+    mp = MotionProducer()
+    d = torch.from_numpy(clip).to(device)
+    change = torch.empty(frames, mp.tiles, device=device)
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        mp.change(d, change, stream)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        mp.change(d, change, stream)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    pairs = frames - 1
+    res = [{"leg": "gpu", "frames": frames, "pairs": pairs, "ms_per_pass": round(ms, 3),
+            "pairs_per_s": round(pairs / (ms / 1e3), 1), "device_status": 0}]
+    try:
+        import cv2
+    except ImportError:
+        res.append({"leg": "cpu_opencv", "unavailable": "cv2 not importable"})
+        mp.close()
+        return res
+    t = time.perf_counter()
+    for f in range(1, cpu_pairs + 1):
+        cv2.calcOpticalFlowFarneback(clip[f - 1], clip[f], None, 0.5, 3, 15, 3, 5, 1.2, 0)
+    dt = (time.perf_counter() - t) / cpu_pairs
+    res.append({"leg": "cpu_opencv", "pairs": cpu_pairs, "ms_per_pair": round(dt * 1e3, 2),
+                "pairs_per_s": round(1.0 / dt, 2), "threads": cv2.getNumThreads(),
+                "opencv": cv2.__version__})
+    mp.close()
+    return res

@@ -196,3 +196,71 @@ def hold_reused_tiles(k: torch.Tensor, v: torch.Tensor, reuse: np.ndarray, *, to
             b = min(a + tile_tokens, (f + 1) * tokens)
             k[a:b] = k[a - tokens:b - tokens]
             v[a:b] = v[a - tokens:b - tokens]
+
+
+# ------------------------------------------------------------ synthetic video
+VIDEO_H, VIDEO_W = 480, 832      # the reference's frame size (30 x 52 cells of 16 px)
+
+
+def synthetic_video(frames: int = 8, *, seed: int = 0, height: int = VIDEO_H, width: int = VIDEO_W,
+                    pan=(0.7, 0.3), zoom: float = 0.004, rot: float = 0.002, blobs: int = 6,
+                    noise: float = 1.0) -> np.ndarray:
+    """Seeded grayscale clip, uint8 [frames, height, width]: a smooth random
+    texture under a camera motion (pan by `pan` pixels, zoom by `zoom` and
+    rotation by `rot` radians per frame about the centre: displacements grow
+    from the centre outwards, so per-tile motion is spread out), plus `blobs`
+    textured discs each moving on its own straight path at 1-6 px/frame,
+    plus N(0, noise) sensor noise; sub-pixel sampling is bilinear.  Stands
+    in for the DAVIS clip the reference's traces/gen_motion_from_video.py
+    reads, which is not available here."""
+    rng = np.random.default_rng(seed)
+
+    def texture(h, w, scale):
+        # band-limited noise: white noise blurred by a separable box cascade
+        t = rng.standard_normal((h + 64, w + 64)).astype(np.float32)
+        for _ in range(3):
+            t = (np.cumsum(np.cumsum(t, 0), 1))
+            t = (t[scale:, scale:] - t[:-scale, scale:] - t[scale:, :-scale] + t[:-scale, :-scale])
+            t /= scale * scale
+        t = t[:h, :w]
+        return (t - t.mean()) / (t.std() + 1e-6)
+
+    H2, W2 = height + 64, width + 64
+    bg = 0.6 * texture(H2, W2, 9) + 0.4 * texture(H2, W2, 3)
+    yy, xx = np.mgrid[0:height, 0:width].astype(np.float32)
+
+    def sample(img, x, y):
+        x0 = np.floor(x).astype(np.int64)
+        y0 = np.floor(y).astype(np.int64)
+        fx, fy = x - x0, y - y0
+        x0 = np.clip(x0, 0, img.shape[1] - 2)
+        y0 = np.clip(y0, 0, img.shape[0] - 2)
+        return ((1 - fx) * (1 - fy) * img[y0, x0] + fx * (1 - fy) * img[y0, x0 + 1] +
+                (1 - fx) * fy * img[y0 + 1, x0] + fx * fy * img[y0 + 1, x0 + 1])
+
+    specs = []
+    for _ in range(blobs):
+        r = rng.uniform(25, 70)
+        c = (rng.uniform(r, width - r), rng.uniform(r, height - r))
+        ang = rng.uniform(0, 2 * np.pi)
+        spd = rng.uniform(1.0, 6.0)
+        tex = texture(int(2 * r) + 8, int(2 * r) + 8, 4)
+        specs.append((r, c, (spd * np.cos(ang), spd * np.sin(ang)), tex, rng.uniform(-1.5, 1.5)))
+    out = np.empty((frames, height, width), np.uint8)
+    cx0, cy0 = width / 2.0, height / 2.0
+    for f in range(frames):
+        sc = (1.0 + zoom) ** (-f)
+        ca, sa = np.cos(-rot * f) * sc, np.sin(-rot * f) * sc
+        ux, uy = xx - cx0, yy - cy0
+        img = sample(bg, cx0 + ca * ux - sa * uy + 32 + pan[0] * f,
+                     cy0 + sa * ux + ca * uy + 32 + pan[1] * f)
+        for r, c, v, tex, off in specs:
+            cx, cy = c[0] + v[0] * f, c[1] + v[1] * f
+            m = (xx - cx) ** 2 + (yy - cy) ** 2 < r * r
+            if m.any():
+                tx = np.clip(xx[m] - cx + r + 4, 0, tex.shape[1] - 1.001)
+                ty = np.clip(yy[m] - cy + r + 4, 0, tex.shape[0] - 1.001)
+                img[m] = sample(tex, tx, ty) + off
+        img = 128 + 40 * img + noise * rng.standard_normal(img.shape)
+        out[f] = np.clip(np.rint(img), 0, 255).astype(np.uint8)
+    return out

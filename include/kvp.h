@@ -143,6 +143,33 @@ int kvp_qkv_project_bf16(const kvp_qkv_io* io, void* stream);
 int kvp_layernorm_bf16(const void* x, const float* gamma, const float* beta, void* y,
                        long long rows, int D, float eps, void* stream);
 
+/* ---- Motion-trace producer on the GPU (traces/gen_motion_from_video.py:
+ * 101-121): dense two-frame optical flow between consecutive frames
+ * (Farnebaeck's polynomial-expansion method, the one the reference calls
+ * through OpenCV with pyr_scale 0.5, levels 3, winsize 15, iterations 3,
+ * poly_n 5, poly_sigma 1.2), per-pixel magnitude, means per cell of the
+ * latent grid and per row-major tile of tile_cells cells.  Frames are uint8
+ * grayscale [frames][height][width] in device memory; height and width must
+ * be multiples of grid_rows and grid_cols. */
+typedef struct {
+    int height, width, levels, winsize, iterations, poly_n;
+    float poly_sigma, pyr_scale;
+    int grid_rows, grid_cols, tile_cells;
+} kvp_motion_params;
+void* kvp_motion_create(const kvp_motion_params* p);   /* NULL on bad parameters / no memory */
+void kvp_motion_destroy(void* m);
+int kvp_motion_tiles(void* m);                         /* tiles per frame */
+/* flow fp32 [2][height][width] (dx plane, dy plane): next(x + d) ~ prev(x) */
+int kvp_motion_flow(void* m, const void* d_prev, const void* d_next, float* d_flow, void* stream);
+/* change fp32 [frames][tiles] on the device: row f >= 1 = mean flow
+ * magnitude per tile between frames f-1 and f, row 0 = row 1 (:117) */
+int kvp_motion_trace(void* m, const void* d_frames, int frames, float* d_change, void* stream);
+/* Host: tau = the percentile (numpy's linear interpolation) of change rows
+ * 1..frames-1; reuse = change < tau except row 0 (all 0); is_static =
+ * change < tau (:119-121, 146-151).  reuse / is_static / tau may be NULL. */
+int kvp_motion_threshold(const float* change, int frames, int tiles, double percentile,
+                         signed char* reuse, signed char* is_static, double* tau);
+
 /* ---- Session: the per-frame admission loop / KVMap emitter of
  * src/run_policy_experiment.cu:156-274 as a library. */
 typedef struct {

@@ -1,6 +1,6 @@
 """Regenerates the committed golden fixtures from the reference's own code.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--only reuse|qkv]
+    python tests/golden/make_golden.py [--ref /root/reference] [--only reuse|qkv|motion]
 
 Needs the reference sources (read, never copied) and is run once, on a host
 where they exist; the tests only read the files it writes:
@@ -34,6 +34,10 @@ where they exist; the tests only read the files it writes:
                           LayerNorm, qkv_proj and view/permute) on seeded
                           inputs (``oracle/qkv.py qkv_params``): sampled rows of h, Q, K, V
                           and per-column sums.  ``--only qkv``.
+* ``motion_ref_clip.csv`` / ``.json`` the reference's own
+                          traces/gen_motion_from_video.py (OpenCV Farneback)
+                          run on a seeded synthetic clip: per-tile change
+                          rates, is_static and reuse, tau.  ``--only motion``.
 """
 
 from __future__ import annotations
@@ -184,10 +188,53 @@ def qkv_fixture(ref: Path):
                         q_colsum=q.sum(0), k_colsum=k.sum(0), v_colsum=v.sum(0))
 
 
+MOTION_SEED, MOTION_FRAMES = 5, 6
+
+
+def motion_fixture(ref: Path):
+    """motion_ref_clip.csv + motion_ref_clip.json: the reference's own
+    traces/gen_motion_from_video.py (OpenCV Farneback + its aggregation) run
+    on the seeded synthetic clip kvp.traces.synthetic_video(MOTION_FRAMES,
+    seed=MOTION_SEED), written as PNG frames.  The script writes a heatmap
+    beside itself, so it runs from a temporary copy (with src/config.py)
+    under /tmp; nothing is written into the reference tree."""
+    import shutil
+    import subprocess
+    import cv2
+    from kvp.traces import synthetic_video
+    work = Path(tempfile.mkdtemp(prefix="kvp_motion_"))
+    try:
+        clip = work / "clip"
+        clip.mkdir()
+        for i, fr in enumerate(synthetic_video(MOTION_FRAMES, seed=MOTION_SEED)):
+            cv2.imwrite(str(clip / f"{i:05d}.png"), fr)
+        (work / "ref" / "traces").mkdir(parents=True)
+        (work / "ref" / "src").mkdir(parents=True)
+        shutil.copy(ref / "traces" / "gen_motion_from_video.py", work / "ref" / "traces")
+        shutil.copy(ref / "src" / "config.py", work / "ref" / "src")
+        (work / "ref" / "src" / "__init__.py").write_text("")
+        out = work / "out"
+        out.mkdir()
+        subprocess.run([sys.executable, str(work / "ref" / "traces" / "gen_motion_from_video.py"),
+                        "--source", str(clip), "--frames", str(MOTION_FRAMES), "--out-dir", str(out),
+                        "--config", str(ref / "configs" / "grounding_config.json")],
+                       check=True, cwd=str(work))
+        shutil.copy(out / "motion_trace_real.csv", HERE / "motion_ref_clip.csv")
+        meta = json.loads((out / "trace_real_meta.json").read_text())
+        (HERE / "motion_ref_clip.json").write_text(json.dumps(
+            {"generator": "tests/golden/make_golden.py --only motion",
+             "clip": f"kvp.traces.synthetic_video({MOTION_FRAMES}, seed={MOTION_SEED})",
+             "opencv": cv2.__version__, "farneback": meta["farneback"],
+             "tau_reuse": meta["tau_reuse"], "reuse_fraction": meta["reuse_fraction_achieved"],
+             "frames": meta["frames"], "num_tiles": meta["num_tiles"]}, indent=1))
+    finally:
+        shutil.rmtree(work, ignore_errors=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=("reuse", "qkv"), default=None,
+    ap.add_argument("--only", choices=("reuse", "qkv", "motion"), default=None,
                     help="regenerate one fixture set only")
     args = ap.parse_args()
     ref = Path(args.ref)
@@ -197,6 +244,9 @@ def main():
         return
     if args.only == "qkv":
         qkv_fixture(ref)
+        return
+    if args.only == "motion":
+        motion_fixture(ref)
         return
     from kvp import traces
 
@@ -294,6 +344,7 @@ def main():
         "golden_per_frame_stats": gm["per_frame_stats"]}, indent=1))
     reuse_fixtures()
     qkv_fixture(ref)
+    motion_fixture(ref)
     print("fixtures written to", HERE)
 
 
