@@ -32,13 +32,16 @@ public:
     int pair_flow(const uint8_t* d_prev, const uint8_t* d_next, float* d_flow, cudaStream_t s);
     // change [frames][tiles] (fp32, device): mean flow magnitude per tile of
     // pair (f-1, f) for f >= 1, row 0 = row 1.  d_frames is uint8
-    // [frames][height][width].
+    // [frames][height][width].  Replays a CUDA graph captured on the first
+    // call for these (d_frames, frames, d_change); a call from inside a
+    // stream capture enqueues the kernels directly.
     int trace(const uint8_t* d_frames, int frames, float* d_change, cudaStream_t s);
 
 private:
     struct Level;
     int load_frame(const uint8_t* d_frame, int slot, cudaStream_t s);
     int flow(int prev_slot, int next_slot, float* d_out, cudaStream_t s);
+    int enqueue_trace(const uint8_t* d_frames, int frames, float* d_change, cudaStream_t s);
 
     MotionParams p_;
     int status_ = 0;
@@ -49,6 +52,13 @@ private:
     float* M_ = nullptr;
     float* flow_[2] = {nullptr, nullptr};
     float* fflow_ = nullptr;
+    // the captured trace pass and the buffers it was captured for
+    cudaStream_t cap_stream_ = nullptr;
+    cudaEvent_t ev_in_ = nullptr, ev_out_ = nullptr;
+    cudaGraphExec_t exec_ = nullptr;
+    const uint8_t* g_frames_ = nullptr;
+    int g_count_ = 0;
+    float* g_change_ = nullptr;
 };
 
 // The reference's threshold (:119-121, :146-151) on host change rates
