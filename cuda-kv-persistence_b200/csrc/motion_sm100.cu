@@ -19,7 +19,8 @@
 // Every image is planar fp32 [channels][h][w] with mirrored borders
 // (reflect-101); one plane of the 480 x 832 frame is 1.6 MB, so a layer's
 // working set stays in L2.  A frame's expansion is kept and serves as the
-// previous frame of the next pair.  The CPU restatement of the same steps
+// previous frame of the next pair.  A whole trace pass is replayed as one
+// CUDA graph (captured on first use for its buffers).  The CPU restatement of the same steps
 // is oracle/motion.py; its agreement with OpenCV's implementation of the
 // method is tested there.
 #include <cuda_runtime.h>
@@ -342,6 +343,13 @@ MotionProducer::MotionProducer(const MotionParams& p) : p_(p) {
 }
 
 MotionProducer::~MotionProducer() {
+    if (exec_) cudaGraphExecDestroy(exec_);
+    if (cap_stream_) {
+        cudaStreamSynchronize(cap_stream_);
+        cudaStreamDestroy(cap_stream_);
+    }
+    if (ev_in_) cudaEventDestroy(ev_in_);
+    if (ev_out_) cudaEventDestroy(ev_out_);
     for (auto& L : levels_)
         for (int i = 0; i < 2; ++i) {
             if (L.img[i]) cudaFree(L.img[i]);
@@ -422,6 +430,50 @@ int MotionProducer::pair_flow(const uint8_t* d_prev, const uint8_t* d_next, floa
 int MotionProducer::trace(const uint8_t* d_frames, int frames, float* d_change, cudaStream_t s) {
     if (status_ != KVP_OK) return status_;
     if (!d_frames || !d_change || frames < 2) return KVP_ERR_ARG;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    KVP_CUDA(cudaStreamIsCapturing(s, &cs));
+    if (cs != cudaStreamCaptureStatusNone) return enqueue_trace(d_frames, frames, d_change, s);
+    // The pass is ~50 small launches per frame pair: replay it as one CUDA
+    // graph (captured once per (frames, count, output)) on a private stream
+    // joined to the caller's by events.
+    if (!cap_stream_) {
+        KVP_CUDA(cudaStreamCreateWithFlags(&cap_stream_, cudaStreamNonBlocking));
+        KVP_CUDA(cudaEventCreateWithFlags(&ev_in_, cudaEventDisableTiming));
+        KVP_CUDA(cudaEventCreateWithFlags(&ev_out_, cudaEventDisableTiming));
+    }
+    if (!exec_ || g_frames_ != d_frames || g_count_ != frames || g_change_ != d_change) {
+        if (exec_) {
+            cudaGraphExecDestroy(exec_);
+            exec_ = nullptr;
+        }
+        KVP_CUDA(cudaStreamBeginCapture(cap_stream_, cudaStreamCaptureModeThreadLocal));
+        const int rc = enqueue_trace(d_frames, frames, d_change, cap_stream_);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(cap_stream_, &g);
+        if (rc != KVP_OK || e != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return rc != KVP_OK ? rc : cuda_status(e, "motion graph capture");
+        }
+        const cudaError_t ei = cudaGraphInstantiate(&exec_, g, 0);
+        cudaGraphDestroy(g);
+        if (ei != cudaSuccess) {
+            exec_ = nullptr;
+            return cuda_status(ei, "motion graph instantiate");
+        }
+        g_frames_ = d_frames;
+        g_count_ = frames;
+        g_change_ = d_change;
+    }
+    KVP_CUDA(cudaEventRecord(ev_in_, s));
+    KVP_CUDA(cudaStreamWaitEvent(cap_stream_, ev_in_, 0));
+    KVP_CUDA(cudaGraphLaunch(exec_, cap_stream_));
+    KVP_CUDA(cudaEventRecord(ev_out_, cap_stream_));
+    KVP_CUDA(cudaStreamWaitEvent(s, ev_out_, 0));
+    return KVP_OK;
+}
+
+int MotionProducer::enqueue_trace(const uint8_t* d_frames, int frames, float* d_change,
+                                  cudaStream_t s) {
     const size_t fbytes = (size_t)p_.height * p_.width;
     // frame f's layers and expansion live in slot f & 1: each frame is
     // expanded once and serves both of its pairs
