@@ -67,3 +67,34 @@ def test_motion_rejects_bad_parameters(cuda):
         MotionProducer(height=481)                  # not a multiple of the 30-row grid
     with pytest.raises(RuntimeError, match="kvp_motion_create"):
         MotionProducer(winsize=14)
+
+
+@pytest.mark.parametrize("params", [
+    dict(levels=1, winsize=9, iterations=2, poly_n=7, poly_sigma=1.5),
+    dict(levels=0, winsize=5, iterations=1, poly_n=5, poly_sigma=1.1),
+])
+def test_gpu_flow_other_parameters_match_oracle(cuda, params):
+    """Non-default flow parameters on a 240 x 416 clip (15 x 26 grid)."""
+    from kvp.motion import MotionProducer
+    from kvp.traces import synthetic_video
+    clip = synthetic_video(3, seed=8, height=240, width=416)
+    mp = MotionProducer(240, 416, grid=(15, 26), **params)
+    d = torch.from_numpy(clip).cuda()
+    out = torch.empty(2, 240, 416, device="cuda")
+    mp.flow(d[1], d[2], out, int(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    want = M.farneback(clip[1], clip[2], pyr_scale=0.5, **params)
+    diff = np.abs(out.cpu().numpy() - want)
+    assert np.median(diff) < 1e-3 and np.percentile(diff, 99) < 2e-2, (params, np.median(diff))
+    change = torch.empty(3, mp.tiles, device="cuda")
+    mp.change(d, change, int(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    got = change.cpu().numpy()
+    mags = [np.hypot(*M.farneback(clip[f - 1], clip[f], pyr_scale=0.5, **params)) for f in (1, 2)]
+    want_change = np.zeros_like(got, dtype=np.float64)
+    for f, m in enumerate(mags, start=1):
+        want_change[f] = M.tile_means(M.cell_means(m, grid=(15, 26)))
+    want_change[0] = want_change[1]
+    rel = np.abs(got - want_change) / np.maximum(want_change, 1e-3)
+    assert rel.max() < 2e-3, (params, rel.max())
+    mp.close()

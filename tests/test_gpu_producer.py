@@ -33,7 +33,7 @@ def _f(t):
     return t.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("rows,D", [(128, 256), (300, 256), (1560, 1536), (4100, 512)])
+@pytest.mark.parametrize("rows,D", [(128, 256), (300, 256), (1560, 1536), (4100, 512), (777, 768)])
 def test_qkv_project_matches_oracle(cuda, rows, D):
     from kvp.attention import read_status
     from kvp.producer import qkv_project
