@@ -442,11 +442,9 @@ struct kvp_qkv_io {
 
 KVP_API int kvp_qkv_project_bf16(const kvp_qkv_io* io, void* stream) {
     if (!io) return kvp::KVP_ERR_ARG;
-    int* st = kvp::status_word();
-    if (!st) return kvp::KVP_ERR_CUDA;
     kvp::QkvIO q{io->x, io->w, io->bias, io->q, io->k, io->v, io->arena, io->kvmap,
                  io->rows, io->map_row0, io->arena_rows, io->D};
-    return kvp::launch_qkv_project_bf16(q, st, (cudaStream_t)stream);
+    return kvp::launch_qkv_project_bf16(q, nullptr, (cudaStream_t)stream);
 }
 
 KVP_API int kvp_layernorm_bf16(const void* x, const float* gamma, const float* beta, void* y,

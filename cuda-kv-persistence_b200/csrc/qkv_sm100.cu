@@ -371,6 +371,8 @@ int launch_qkv_project_bf16(const QkvIO& io, int* d_status, cudaStream_t stream)
                   "aligned buffers, a map needs an arena)");
         return KVP_ERR_ARG;
     }
+    if (!d_status) d_status = status_word();   // after the argument checks: they need no device
+    if (!d_status) return KVP_ERR_CUDA;
     static PerDeviceOnce setup;
     const int rc_setup = setup([](int) {
         KVP_CUDA(cudaFuncSetAttribute(qkv_proj_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

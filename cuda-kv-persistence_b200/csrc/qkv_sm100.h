@@ -27,6 +27,7 @@ struct QkvIO {
     int D;
 };
 
+// d_status null = the current device's status word.
 int launch_qkv_project_bf16(const QkvIO& io, int* d_status, cudaStream_t stream);
 
 // y = LayerNorm(x) * gamma + beta per row (bf16 in and out, fp32 statistics).
