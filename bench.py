@@ -440,6 +440,10 @@ def run_matrix(args) -> int:
                                       streaming=args.streaming):
             print(json.dumps({"metric": "config5 cell", "streaming": args.streaming, **row}),
                   flush=True)
+    elif args.matrix == 9:
+        for row in matrix.run_sdpa_compare(reps=max(1, args.reps), seed=args.seed):
+            print(json.dumps({"metric": "intra-frame attention, 21 x 1560 tokens x 12 heads", **row}),
+                  flush=True)
     elif args.matrix == 8:
         for row in matrix.run_motion(reps=max(1, args.reps), seed=args.seed):
             print(json.dumps({"metric": "motion-trace producer, 480x832 frame pairs", **row}),
@@ -477,7 +481,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--matrix", type=int, choices=[2, 3, 5, 6, 7, 8], default=0,
+    ap.add_argument("--matrix", type=int, choices=[2, 3, 5, 6, 7, 8, 9], default=0,
                     help="instead of the config-4 line: config 5 (policy x budget x regime, one "
                          "JSON line per cell), config 3 (50 frames x 30 layers, window 5; None "
                          "and ReuseWeighted) or config 2 (one line), per-frame cross attention; "
@@ -485,7 +489,9 @@ def main() -> int:
                          "against re-staging every frame, per trace x budget x policy; 7: one "
                          "layer's K/V production for config 4 (LayerNorm + tcgen05 QKV producer "
                          "writing the arena, against cuBLAS + gather); 8: the motion-trace "
-                         "producer (GPU optical flow + tile rates) against OpenCV on the host")
+                         "producer (GPU optical flow + tile rates) against OpenCV on the host; 9: "
+                         "the attention kernel against torch SDPA backends (cuDNN first) on "
+                         "intra-frame attention")
     ap.add_argument("--reps", type=int, default=3, help="repetitions per cell with --matrix (ABBA)")
     ap.add_argument("--streaming", action="store_true",
                     help="with --matrix 3 or 5: streaming arena (sticky slots, LIFO reuse) instead of "

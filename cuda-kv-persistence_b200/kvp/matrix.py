@@ -526,3 +526,54 @@ def run_motion(*, frames: int = 20, reps: int = 5, seed: int = 0, cpu_pairs: int
                 "opencv": cv2.__version__})
     mp.close()
     return res
+
+
+def run_sdpa_compare(*, reps: int = 20, warmup: int = 3, frames: int = 21, tokens: int = 1560,
+                     heads: int = 12, seed: int = 0, device="cuda") -> list[dict]:
+    """The tcgen05 kernel against torch's scaled_dot_product_attention
+    backends (cuDNN's fused attention first) on the same work: intra-frame
+    attention of `frames` frames x `tokens` tokens x `heads` heads, bf16,
+    no mask (per frame, softmax over its own tokens).  Inputs are laid out
+    for each side outside the timed region."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    import torch.nn.functional as Fn
+    D = heads * 128
+    q, k, v = qkv(frames * tokens, D, seed=seed, device=device)
+    out = torch.empty_like(q)
+    flop = 4.0 * tokens * tokens * 128 * heads * frames
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    read_status()
+    ms = timed(lambda: attn_bf16(q, k, v, out, tokens=tokens, frames=frames, heads=heads,
+                                 mode="intra", stream=stream))
+    res = [{"leg": "kvp tcgen05", "ms": round(ms, 4), "tflops": round(flop / (ms / 1e3) / 1e12, 1),
+            "device_status": read_status()}]
+    to4 = lambda t: t.view(frames, tokens, heads, 128).transpose(1, 2).contiguous()
+    q4, k4, v4 = to4(q), to4(k), to4(v)
+    ref = out.view(frames, tokens, heads, 128).transpose(1, 2).float()
+    for name, be in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION),
+                     ("efficient", SDPBackend.EFFICIENT_ATTENTION)):
+        try:
+            with sdpa_kernel(be):
+                o4 = Fn.scaled_dot_product_attention(q4, k4, v4)
+                torch.cuda.synchronize()
+                ms = timed(lambda: Fn.scaled_dot_product_attention(q4, k4, v4))
+            err = float((o4.float() - ref).abs().max())
+            res.append({"leg": f"sdpa {name}", "ms": round(ms, 4),
+                        "tflops": round(flop / (ms / 1e3) / 1e12, 1), "max_abs_vs_kvp": round(err, 5)})
+        except Exception as e:  # backend not available for this device / layout
+            res.append({"leg": f"sdpa {name}", "unavailable": str(e).splitlines()[0][:160]})
+    return res
