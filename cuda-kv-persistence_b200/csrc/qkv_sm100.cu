@@ -355,6 +355,71 @@ layernorm_bf16_kernel(const __nv_bfloat16* __restrict__ x, const float* __restri
     }
 }
 
+// Same LayerNorm with the row held in registers: each lane keeps its
+// kChunks 16-byte chunks, so the row is read from memory once (D = 256 *
+// kChunks).  Statistics in the same order as the three-pass kernel.
+template <int kChunks>
+__global__ void __launch_bounds__(256)
+layernorm_bf16_reg_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma,
+                          const float* __restrict__ beta, __nv_bfloat16* __restrict__ y,
+                          long long rows, float eps) {
+    constexpr int D = kChunks * 256;
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * D);
+    uint4* yr = reinterpret_cast<uint4*>(y + row * D);
+    uint4 u[kChunks];
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) u[i] = xr[lane + 32 * i];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            s += f.x + f.y;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / (float)D;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            ss += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rstd = 1.f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+        const int c = lane + 32 * i;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[i]);
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * c);
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * c + 1);
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta) + 2 * c);
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta) + 2 * c + 1);
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        uint4 o;
+        uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            op[j] = pack_bf16((f.x - mean) * rstd * g[2 * j] + b[2 * j],
+                              (f.y - mean) * rstd * g[2 * j + 1] + b[2 * j + 1]);
+        }
+        yr[c] = o;
+    }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -423,8 +488,19 @@ int launch_layernorm_bf16(const void* x, const float* gamma, const float* beta, 
         return KVP_ERR_ARG;
     }
     const long long blocks = (rows + 7) / 8;
-    layernorm_bf16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), gamma, beta, static_cast<__nv_bfloat16*>(y), rows, D, eps);
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    auto* yb = static_cast<__nv_bfloat16*>(y);
+    switch (D % 256 == 0 ? D / 256 : 0) {
+        case 1: layernorm_bf16_reg_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, eps); break;
+        case 2: layernorm_bf16_reg_kernel<2><<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, eps); break;
+        case 3: layernorm_bf16_reg_kernel<3><<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, eps); break;
+        case 4: layernorm_bf16_reg_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, eps); break;
+        case 5: layernorm_bf16_reg_kernel<5><<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, eps); break;
+        case 6: layernorm_bf16_reg_kernel<6><<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, eps); break;
+        case 8: layernorm_bf16_reg_kernel<8><<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, eps); break;
+        default:
+            layernorm_bf16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(xb, gamma, beta, yb, rows, D, eps);
+    }
     KVP_CUDA(cudaGetLastError());
     return KVP_OK;
 }

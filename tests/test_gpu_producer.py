@@ -93,8 +93,10 @@ def test_qkv_project_writes_mapped_rows_to_arena(cuda):
     assert torch.equal(q, q2) and torch.equal(k, k2) and torch.equal(v, v2)
 
 
-@pytest.mark.parametrize("rows,D", [(333, 256), (1560, 1536)])
+@pytest.mark.parametrize("rows,D", [(333, 256), (1560, 1536), (77, 2048), (100, 200)])
 def test_layernorm_matches_oracle(cuda, rows, D):
+    """Register-resident rows for D a multiple of 256 (up to 2048), the
+    three-pass kernel otherwise (D = 200)."""
     from kvp.producer import layernorm
     rng = np.random.default_rng(rows)
     x = _bf(3.0 + 2.0 * rng.standard_normal((rows, D)))
