@@ -442,8 +442,7 @@ def run_matrix(args) -> int:
                   flush=True)
     elif args.matrix == 9:
         for row in matrix.run_sdpa_compare(reps=max(1, args.reps), seed=args.seed):
-            print(json.dumps({"metric": "intra-frame attention, 21 x 1560 tokens x 12 heads", **row}),
-                  flush=True)
+            print(json.dumps({"metric": "intra-frame attention, 12 heads, bf16", **row}), flush=True)
     elif args.matrix == 8:
         for row in matrix.run_motion(reps=max(1, args.reps), seed=args.seed):
             print(json.dumps({"metric": "motion-trace producer, 480x832 frame pairs", **row}),

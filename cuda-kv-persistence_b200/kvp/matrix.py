@@ -528,13 +528,22 @@ def run_motion(*, frames: int = 20, reps: int = 5, seed: int = 0, cpu_pairs: int
     return res
 
 
-def run_sdpa_compare(*, reps: int = 20, warmup: int = 3, frames: int = 21, tokens: int = 1560,
+def run_sdpa_compare(*, reps: int = 20, warmup: int = 3, shapes=((21, 1560), (2, 16380)),
                      heads: int = 12, seed: int = 0, device="cuda") -> list[dict]:
     """The tcgen05 kernel against torch's scaled_dot_product_attention
-    backends (cuDNN's fused attention first) on the same work: intra-frame
-    attention of `frames` frames x `tokens` tokens x `heads` heads, bf16,
-    no mask (per frame, softmax over its own tokens).  Inputs are laid out
-    for each side outside the timed region."""
+    backends (cuDNN's fused attention first) on the same work, per (frames,
+    tokens) shape: intra-frame attention of `frames` frames x `tokens`
+    tokens x `heads` heads, bf16, no mask (per frame, softmax over its own
+    tokens).  Inputs are laid out for each side outside the timed region."""
+    res = []
+    for frames, tokens in shapes:
+        for r in _sdpa_compare_one(reps=reps, warmup=warmup, frames=frames, tokens=tokens,
+                                   heads=heads, seed=seed, device=device):
+            res.append({"frames": frames, "tokens": tokens, **r})
+    return res
+
+
+def _sdpa_compare_one(*, reps, warmup, frames, tokens, heads, seed, device):
     from torch.nn.attention import SDPBackend, sdpa_kernel
     import torch.nn.functional as Fn
     D = heads * 128
