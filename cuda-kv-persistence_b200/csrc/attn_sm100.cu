@@ -198,26 +198,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// 2^x on the FMA/ALU pipes: x = n + f with n = round(x) and f in [-1/2, 1/2],
-// 2^f by a cubic fitted here by iteratively reweighted least squares on the
-// relative error (max relative error 1.4e-4 over x in [-126, 8], against bf16's
-// 3.9e-3 rounding of P), 2^n added to the exponent bits.  Inputs below -126
-// are clamped to -126 (the result stays a positive number below 2^-125,
-// negligible in the row sum and against any unmasked P; -inf lands there
-// too), inputs above 127 to 127 (a finite 2^127-ish value, so an overgrown
-// speculative exponent still shows up in the row sum instead of wrapping
-// the exponent bits).
-__device__ __forceinline__ float ex2_poly(float x) {
-    x = fminf(fmaxf(x, -126.f), 127.f);
-    const float t = x + 12582912.f;           // 1.5 * 2^23: round to nearest integer
-    const float f = x - (t - 12582912.f);
-    float p = fmaf(5.517162719e-02f, f, 2.426111432e-01f);
-    p = fmaf(p, f, 6.932609953e-01f);
-    p = fmaf(p, f, 9.999280725e-01f);
-    const int n = __float_as_int(t) - 0x4B400000;
-    return __int_as_float(__float_as_int(p) + (n << 23));
-}
-
 // Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot per pair).
 __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
     uint64_t r;
@@ -242,7 +222,15 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
-// ex2_poly on a pair, the arithmetic in f32x2 (same fit, same clamps).
+// 2^x for a pair on the FMA/ALU pipes (f32x2 arithmetic): x = n + f with
+// n = round(x) and f in [-1/2, 1/2], 2^f by a cubic fitted here by iteratively reweighted least squares on the
+// relative error (max relative error 1.4e-4 over x in [-126, 8], against bf16's
+// 3.9e-3 rounding of P), 2^n added to the exponent bits.  Inputs below -126
+// are clamped to -126 (the result stays a positive number below 2^-125,
+// negligible in the row sum and against any unmasked P; -inf lands there
+// too), inputs above 127 to 127 (a finite 2^127-ish value, so an overgrown
+// speculative exponent still shows up in the row sum instead of wrapping
+// the exponent bits).
 __device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
     const uint64_t x = f2_pack(fminf(fmaxf(x0, -126.f), 127.f), fminf(fmaxf(x1, -126.f), 127.f));
     const uint64_t magic = f2_pack(12582912.f, 12582912.f);
