@@ -6,8 +6,8 @@
 // tiles that dropped out (streaming) -> stage the selected tiles' rows in
 // policy order -> KVMap[row] = arena slot.  Admission, slot numbers and byte
 // counts are bit-exact with the reference for intra and cross modes; the
-// sliding window (cross, window > 0) and the stack mode are extensions
-// defined in DESIGN.md terms below:
+// sliding window (cross, window > 0), the stack mode and the reuse mode are
+// extensions, defined as follows:
 //   * window W: frame f's candidates are the tiles of frames
 //     [max(0, f-W+1), f]; ReuseWeighted counts remaining sweeps from that
 //     first frame (total_frames - base); ids are offset to absolute gids;

@@ -5,9 +5,12 @@
   with motion-coupled K/V drift) with the same constants and the same draw
   order from one seeded torch.Generator, so seed 42 / 8 frames reproduces
   the reference's trace_meta_8f.json and golden_meta.json statistics.
-* ``motion_config{1..5}`` are the seeded motion generators of the BASELINE
-  configs (new; defined in DESIGN.md).  Each uses its own
+* ``motion_config{1..5}`` are seeded motion generators for the five
+  benchmark configurations (the reference ships no generator for them; each
+  docstring states its distribution).  Each uses its own
   ``torch.Generator().manual_seed(seed)``; Q/K/V come from ``qkv``.
+* ``reuse_flags``, ``hold_reused_tiles`` and ``synthetic_video`` feed the
+  temporal-reuse and motion-producer paths.
 * ``write_motion_csv`` writes the reference CSV
   (frame_id,tile_id,motion_score,is_static,token_start,token_count) with
   6-decimal scores, the text the reference driver parses with "%f".
