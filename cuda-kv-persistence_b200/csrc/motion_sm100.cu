@@ -15,7 +15,9 @@
 //       A = (A1(x) + A2(x~)) / 2, db = (b1(x) - b2(x~)) / 2 + A d~,
 //       x~ = x + d~ (R2 sampled bilinearly)
 //   d = (box mean of G)^-1 (box mean of h), winsize x winsize, `iterations`
-//       times, M refreshed from the new d between iterations
+//       times, M refreshed from the new d between iterations (one
+//       shared-memory tile kernel per iteration: both box passes, the solve
+//       and the refresh)
 // Every image is planar fp32 [channels][h][w] with mirrored borders
 // (reflect-101); one plane of the 480 x 832 frame is 1.6 MB, so a layer's
 // working set stays in L2.  A frame's expansion is kept and serves as the
@@ -177,46 +179,66 @@ __global__ void update_matrices_kernel(const float* __restrict__ R1, const float
     matrices_at(R1, R2, H, W, x, y, flow[o], flow[plane + o], M);
 }
 
-// Vertical box mean of the 5 planes of M.
-__global__ void box_v_kernel(const float* __restrict__ M, float* __restrict__ T, int H, int W, int r,
-                             float inv) {
-    const int x = blockIdx.x * blockDim.x + threadIdx.x;
-    const int y = blockIdx.y;
-    if (x >= W) return;
-    const size_t plane = (size_t)H * W;
-    float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int k = -r; k <= r; ++k) {
-        const size_t o = (size_t)mirror(y + k, H) * W + x;
-#pragma unroll
-        for (int c = 0; c < 5; ++c) acc[c] += M[c * plane + o];
-    }
-#pragma unroll
-    for (int c = 0; c < 5; ++c) T[c * plane + (size_t)y * W + x] = acc[c] * inv;
+// One displacement iteration for a kTH x kTW tile of pixels: the tile's
+// window region of the 5 planes of M (mirrored at the image edges) is staged
+// in shared memory, summed vertically then horizontally there, and each
+// pixel solves its 2x2 system -> flow and, when `update`, writes M for the
+// new flow into Mout (a second buffer: neighbouring tiles still read Min).
+constexpr int kTW = 32, kTH = 16;
+constexpr int kBoxMaxR = 15;
+__host__ __device__ constexpr size_t box_tile_smem_floats(int r) {
+    return (size_t)5 * (kTH + 2 * r) * (kTW + 2 * r) + (size_t)5 * kTH * (kTW + 2 * r);
 }
 
-// Horizontal box mean, 2x2 solve -> flow, and (update != 0) M for the new flow.
-__global__ void box_h_solve_kernel(const float* __restrict__ T, const float* __restrict__ R1,
-                                   const float* __restrict__ R2, float* __restrict__ flow,
-                                   float* __restrict__ M, int H, int W, int r, float inv, int update) {
-    const int x = blockIdx.x * blockDim.x + threadIdx.x;
-    const int y = blockIdx.y;
-    if (x >= W) return;
-    const size_t plane = (size_t)H * W, row = (size_t)y * W;
-    float g[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int k = -r; k <= r; ++k) {
-        const size_t o = row + mirror(x + k, W);
+__global__ void __launch_bounds__(256)
+box_solve_tile_kernel(const float* __restrict__ Min, const float* __restrict__ R1,
+                      const float* __restrict__ R2, float* __restrict__ flow,
+                      float* __restrict__ Mout, int H, int W, int r, float inv2, int update) {
+    extern __shared__ float sh[];
+    const int IW = kTW + 2 * r, IH = kTH + 2 * r;
+    float* in = sh;                                  // [5][IH][IW]
+    float* vs = sh + (size_t)5 * IH * IW;            // [5][kTH][IW]
+    const int x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
+    const size_t plane = (size_t)H * W;
+    for (int idx = threadIdx.x; idx < IH * IW; idx += blockDim.x) {
+        const int i = idx / IW, j = idx - (idx / IW) * IW;
+        const size_t o = (size_t)mirror(y0 - r + i, H) * W + mirror(x0 - r + j, W);
 #pragma unroll
-        for (int c = 0; c < 5; ++c) g[c] += T[c * plane + o];
+        for (int c = 0; c < 5; ++c) in[c * IH * IW + idx] = Min[c * plane + o];
     }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kTH * IW; idx += blockDim.x) {
+        const int i = idx / IW, j = idx - (idx / IW) * IW;
 #pragma unroll
-    for (int c = 0; c < 5; ++c) g[c] *= inv;
-    const float det = g[0] * g[2] - g[1] * g[1];
-    const float idet = 1.f / (det + 1e-3f);
-    const float dx = (g[2] * g[3] - g[1] * g[4]) * idet;
-    const float dy = (g[0] * g[4] - g[1] * g[3]) * idet;
-    flow[row + x] = dx;
-    flow[plane + row + x] = dy;
-    if (update) matrices_at(R1, R2, H, W, x, y, dx, dy, M);
+        for (int c = 0; c < 5; ++c) {
+            const float* col = in + c * IH * IW + i * IW + j;
+            float a = 0.f;
+            for (int m = 0; m <= 2 * r; ++m) a += col[m * IW];
+            vs[c * kTH * IW + idx] = a;
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < kTH * kTW; idx += blockDim.x) {
+        const int i = idx / kTW, j = idx - (idx / kTW) * kTW;
+        const int x = x0 + j, y = y0 + i;
+        if (x >= W || y >= H) continue;
+        float g[5];
+#pragma unroll
+        for (int c = 0; c < 5; ++c) {
+            const float* row = vs + c * kTH * IW + i * IW + j;
+            float a = 0.f;
+            for (int m = 0; m <= 2 * r; ++m) a += row[m];
+            g[c] = a * inv2;
+        }
+        const float det = g[0] * g[2] - g[1] * g[1];
+        const float idet = 1.f / (det + 1e-3f);
+        const float dx = (g[2] * g[3] - g[1] * g[4]) * idet;
+        const float dy = (g[0] * g[4] - g[1] * g[3]) * idet;
+        const size_t o = (size_t)y * W + x;
+        flow[o] = dx;
+        flow[plane + o] = dy;
+        if (update) matrices_at(R1, R2, H, W, x, y, dx, dy, Mout);
+    }
 }
 
 // change[t] = mean |flow| over tile t's cells (cell = ch x cw pixels of the
@@ -307,7 +329,7 @@ struct MotionProducer::Level {
 
 MotionProducer::MotionProducer(const MotionParams& p) : p_(p) {
     if (p.height < 32 || p.width < 32 || p.levels < 0 || p.levels > 8 || p.winsize < 3 ||
-        p.winsize % 2 == 0 || p.iterations < 1 || p.poly_n < 3 || p.poly_n % 2 == 0 ||
+        p.winsize % 2 == 0 || p.winsize / 2 > kBoxMaxR || p.iterations < 1 || p.poly_n < 3 || p.poly_n % 2 == 0 ||
         p.poly_n > 15 || !(p.poly_sigma > 0) || !(p.pyr_scale > 0 && p.pyr_scale < 1) ||
         p.grid_rows <= 0 || p.grid_cols <= 0 || p.height % p.grid_rows || p.width % p.grid_cols ||
         p.tile_cells <= 0) {
@@ -336,6 +358,10 @@ MotionProducer::MotionProducer(const MotionParams& p) : p_(p) {
     if (e == cudaSuccess) e = cudaMalloc(&tmp_, 5 * full * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&tmp2_, 5 * full * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&M_, 5 * full * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&M2_, 5 * full * sizeof(float));
+    if (e == cudaSuccess && box_tile_smem_floats(p.winsize / 2) * sizeof(float) > 48 * 1024)
+        e = cudaFuncSetAttribute(box_solve_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(box_tile_smem_floats(p.winsize / 2) * sizeof(float)));
     if (e == cudaSuccess) e = cudaMalloc(&flow_[0], 2 * full * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&flow_[1], 2 * full * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&fflow_, 2 * full * sizeof(float));
@@ -355,7 +381,7 @@ MotionProducer::~MotionProducer() {
             if (L.img[i]) cudaFree(L.img[i]);
             if (L.R[i]) cudaFree(L.R[i]);
         }
-    for (float* p : {tmp_, tmp2_, M_, flow_[0], flow_[1], fflow_})
+    for (float* p : {tmp_, tmp2_, M_, M2_, flow_[0], flow_[1], fflow_})
         if (p) cudaFree(p);
 }
 
@@ -407,11 +433,12 @@ int MotionProducer::flow(int prev_slot, int next_slot, float* d_out, cudaStream_
         const float* R1 = L.R[prev_slot];
         const float* R2 = L.R[next_slot];
         update_matrices_kernel<<<grid_of(L.h, L.w), 128, 0, s>>>(R1, R2, fl, M_, L.h, L.w);
-        for (int it = 0; it < p_.iterations; ++it) {
-            box_v_kernel<<<grid_of(L.h, L.w), 128, 0, s>>>(M_, tmp_, L.h, L.w, r, inv);
-            box_h_solve_kernel<<<grid_of(L.h, L.w), 128, 0, s>>>(tmp_, R1, R2, fl, M_, L.h, L.w, r, inv,
-                                                                  it < p_.iterations - 1);
-        }
+        const dim3 gt((unsigned)((L.w + kTW - 1) / kTW), (unsigned)((L.h + kTH - 1) / kTH));
+        float* Mb[2] = {M_, M2_};
+        for (int it = 0; it < p_.iterations; ++it)
+            box_solve_tile_kernel<<<gt, 256, box_tile_smem_floats(r) * sizeof(float), s>>>(
+                Mb[it & 1], R1, R2, fl, Mb[(it + 1) & 1], L.h, L.w, r, inv * inv,
+                it < p_.iterations - 1);
     }
     KVP_CUDA(cudaGetLastError());
     return KVP_OK;

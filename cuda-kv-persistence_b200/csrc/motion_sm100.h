@@ -50,6 +50,7 @@ private:
     float* tmp_ = nullptr;
     float* tmp2_ = nullptr;
     float* M_ = nullptr;
+    float* M2_ = nullptr;
     float* flow_[2] = {nullptr, nullptr};
     float* fflow_ = nullptr;
     // the captured trace pass and the buffers it was captured for
