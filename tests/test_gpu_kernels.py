@@ -253,3 +253,29 @@ def test_bf16_key_split_matches_oracle(cuda, monkeypatch, splits):
     b = _run_bf16(q, k, v, None, None, tokens=T, frames=F, heads=H, mode="causal")
     assert np.array_equal(a, b)
     check_bf16(a, want, ("split", splits))
+
+
+@pytest.mark.parametrize("mode,flat", [("causal", False), ("causal", True), ("intra", False)])
+def test_bf16_peaked_scores_exercise_rescale(cuda, mode, flat):
+    """Scores with a wide, growing range: unit-scale Q, and K rows whose size
+    ramps up along the key index, so a row's maximum keeps rising from tile
+    to tile by more than the lazy-rescale threshold (8 in log2 units).  The
+    softmax then takes its recompute-and-rescale path on most steps; results
+    must still match the oracle within the bf16 gates, mapped or not."""
+    F, T, H = 3, 300, 2
+    D = H * 128
+    rng = np.random.default_rng(31)
+    q = bf16_round(rng.standard_normal((F * T, D)).astype(np.float32))
+    # about 3/4 of the rows see their max rise by > 8 (log2) from the first
+    # key tile to the second, 1/5 again from the second to the third
+    ramp = (0.1 + 8.0 * (np.arange(F * T) % T) / T).astype(np.float32)[:, None]
+    k = bf16_round((rng.standard_normal((F * T, D)) * ramp).astype(np.float32))
+    v = bf16_round(rng.standard_normal((F * T, D)).astype(np.float32))
+    want = attention_frames(q, k, v, frames=F, tokens=T, heads=H, head_dim=128,
+                            mode="intra" if mode == "intra" else "cross")
+    m = _scattered_map(F * T, 250, seed=32)
+    arena = build_arena(k, v, m, 250)
+    a = _run_bf16(q, k, v, m, arena, tokens=T, frames=F, heads=H, mode=mode, flat=flat)
+    b = _run_bf16(q, k, v, None, None, tokens=T, frames=F, heads=H, mode=mode, flat=flat)
+    assert np.array_equal(a, b)
+    check_bf16(a, want, ("peaked", mode, flat))
