@@ -79,6 +79,10 @@ public:
     bool streaming_apply_window();
     void streaming_end();
     size_t streaming_staged_bytes() const { return staged_bytes_; }
+    // Counts a re-copy of `bytes` into slots already held (what
+    // streaming_reserve does for a held row with changed = true), for callers
+    // that know the slots without looking them up.
+    void streaming_count_restage(size_t bytes) { staged_bytes_ += bytes; }
 
     // ---- B200 additions
     // Slot accounting without a copy (the caller stages rows itself, e.g. a

@@ -209,6 +209,10 @@ int Session::plan_reuse(int f, const float* scores_flat, const int8_t* reuse_fla
     std::fill(selected_.begin(), selected_.begin() + nt_, 0);
     for (int i = 0; i < count; ++i)
         if (ids_[i] >= 0 && ids_[i] < nt_) selected_[(size_t)ids_[i]] = 1;
+    if (tile_full_.size() != (size_t)nt_) {
+        tile_full_.assign((size_t)nt_, 0);
+        tile_slots_.assign((size_t)(nt_ * c_.tile_tokens), -1);
+    }
     if (persist && f > 0) {
         for (int64_t tile = 0; tile < nt_; ++tile) {
             if (!prev_selected_[(size_t)tile] || selected_[(size_t)tile]) continue;
@@ -218,6 +222,7 @@ int Session::plan_reuse(int f, const float* scores_flat, const int8_t* reuse_fla
             // the next admitted tile in ascending order, so its 8-row groups
             // stay single ascending runs the kernel stages with TMA boxes.
             for (int64_t r = cnt - 1; r >= 0; --r) mgr_->streaming_release((long)(t0 + r));
+            tile_full_[(size_t)tile] = 0;
         }
     }
     int64_t* map = map_.data() + (int64_t)f * c_.tokens;
@@ -229,6 +234,25 @@ int Session::plan_reuse(int f, const float* scores_flat, const int8_t* reuse_fla
         const int64_t t0 = layout_.tile_start(tile);
         const int64_t cnt = layout_.tile_count(tile);
         const bool changed = !(reuse_flat && reuse_flat[(int64_t)f * nt_ + tile]);
+        int64_t* cached = tile_slots_.data() + tile * c_.tile_tokens;
+        if (tile_full_[(size_t)tile]) {
+            // Every row holds its slot: a sticky hit changes no manager
+            // state, a re-copy only counts its bytes (streaming_reserve with
+            // a held row), so neither needs the per-row lookup.
+            for (int64_t r = 0; r < cnt; ++r) map[t0 + r] = cached[r];
+            if (!changed) {
+                info_.hits += (int)cnt;
+            } else {
+                mgr_->streaming_count_restage((size_t)(cnt * 2 * row_kv_bytes_));
+                info_.restaged += (int)cnt;
+                for (int64_t r = 0; r < cnt; ++r) {
+                    pairs_.push_back((int32_t)((int64_t)f * c_.tokens + t0 + r));
+                    pairs_.push_back((int32_t)cached[r]);
+                }
+            }
+            ++tiles_ok;
+            continue;
+        }
         bool all = true;
         for (int64_t r = 0; r < cnt && all; ++r) {
             long slot = -1;
@@ -237,12 +261,16 @@ int Session::plan_reuse(int f, const float* scores_flat, const int8_t* reuse_fla
                                           &copy, &held);
             if (!all) break;
             map[t0 + r] = slot;
+            cached[r] = slot;
             if (!copy) { ++info_.hits; continue; }
             if (held) ++info_.restaged;
             pairs_.push_back((int32_t)((int64_t)f * c_.tokens + t0 + r));
             pairs_.push_back((int32_t)slot);
         }
-        if (all) ++tiles_ok;
+        if (all) {
+            ++tiles_ok;
+            tile_full_[(size_t)tile] = 1;
+        }
     }
     info_.staged_tiles = tiles_ok;
     info_.copies = (int)(pairs_.size() / 2);

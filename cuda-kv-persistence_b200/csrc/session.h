@@ -134,6 +134,10 @@ private:
     std::vector<long> ids_;
     std::vector<long> sel_ids_;
     std::vector<char> selected_, prev_selected_;
+    // reuse mode: the slots of each tile whose rows all hold one (tile_full_),
+    // so kept tiles map and re-copy without a lookup per row
+    std::vector<int64_t> tile_slots_;
+    std::vector<char> tile_full_;
     int64_t prev_len_ = 0;
     int last_frame_ = -1;
     bool finished_ = false;
