@@ -34,8 +34,6 @@ def _flags(src: Path) -> list[str]:
             "-fPIC,-fvisibility=hidden,-ffp-contract=off", "-I", str(CSRC)]
     if src.suffix == ".cu":
         base += ["--expt-relaxed-constexpr", "-Xptxas", "-v" if os.environ.get("KVP_PTXAS_V") else "-O3"]
-    else:
-        base += ["-x", "cu"] if False else []
     return base
 
 

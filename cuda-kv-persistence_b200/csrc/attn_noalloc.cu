@@ -1,11 +1,12 @@
 // kvp_attn_bf16_noalloc: the bf16 tcgen05 remapped attention for callers
 // that must not allocate device memory.
 //
-// Who needs it: code that runs inside a CUDA stream capture (allocation is
-// not allowed while capturing), hosts that hand all device memory to one
-// pre-planned pool or custom allocator and forbid stray cudaMalloc calls,
-// and latency-critical serving loops that cannot afford the first-call
-// allocation stall.  kvp_attn_bf16 allocates a small device status word on
+// Who needs it: hosts that hand all device memory to one pre-planned pool
+// or custom allocator and forbid stray cudaMalloc calls (an embedding
+// runtime that budgets every byte of HBM up front, or a caching allocator
+// that has already reserved the device), and latency-critical serving
+// loops that cannot afford the first-call allocation stall (cudaMalloc
+// synchronises the device).  kvp_attn_bf16 allocates a small device status word on
 // its first call per device and expects the KVMap already in device memory,
 // so those callers cannot use it.
 //

@@ -98,9 +98,9 @@ typedef struct {
 int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
 
 /* No counterpart in the reference.  kvp_attn_bf16 for callers that cannot
- * allocate device memory -- code inside a stream capture, hosts whose
- * allocator owns all device memory, serving loops that cannot take a
- * first-call cudaMalloc.  Nothing is allocated: the status word and a device
+ * allocate device memory -- hosts whose allocator owns all device memory
+ * and forbids stray cudaMalloc calls, serving loops that cannot take the
+ * device-wide synchronisation of a first-call cudaMalloc.  Nothing is allocated: the status word and a device
  * copy of the KVMap, which the caller passes in HOST memory (host_kvmap,
  * int64, (q_frame0+frames)*tokens rows, at most 65,536; NULL = no remap;
  * io->kvmap must be NULL), live in a static device array of ~512 KB that

@@ -1,8 +1,9 @@
 """kvp_attn_bf16_noalloc against kvp_attn_bf16, through the C ABI.
 
 The no-alloc entry point exists for callers that may not allocate device
-memory (inside a stream capture, under an allocator that owns all device
-memory, in a serving loop that cannot take a first-call cudaMalloc).  Its
+memory (under an allocator that owns all device memory and forbids stray
+cudaMalloc calls, or in a serving loop that cannot take the device-wide
+synchronisation of a first-call cudaMalloc).  Its
 scratch -- the status word and a device copy of the host-side KVMap -- is a
 static device array shared by every call.  This file runs last so that a
 failure here never hides the other GPU tests; it must pass both alone in a
