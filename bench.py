@@ -359,7 +359,18 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
 
 def run_e2e(args, stack, scores, dev, stream, world, local_rank):
     """Same step with Q/K/V copied from pinned host memory and O copied back,
-    per layer chunk: H2D(chunk c+1) overlaps compute(c), D2H(c) overlaps compute(c+1)."""
+    per layer chunk: H2D(chunk c+1) overlaps compute(c), D2H(c) overlaps
+    compute(c+1).
+
+    Every host-to-device copy of a step -- the KVMap upload first, then the
+    Q/K/V chunks -- goes through the one copy stream, in the order the
+    compute needs it.  A small copy queued on the compute stream instead
+    waits behind every bulk copy already queued on the copy stream (the copy
+    engine does not interleave them), which held each step's first layer
+    back until the copy stream had drained.  The copy stream waits for the
+    previous step's last layer before it overwrites the map and the chunk
+    buffers; each layer waits for the previous step's read-back of its
+    output buffer."""
     import torch
     import torch.distributed as dist
     h2d = torch.cuda.Stream(device=dev)
@@ -369,30 +380,36 @@ def run_e2e(args, stack, scores, dev, stream, world, local_rank):
         host.append(tuple(t.to("cpu").pin_memory() for t in (c.q, c.k, c.v)) +
                     (torch.empty(c.o.shape, dtype=torch.bfloat16).pin_memory(),))
     sp = int(stream.cuda_stream)
+    hp = int(h2d.cuda_stream)
     h2d_bytes = sum(sum(t.numel() * 2 for t in h[:3]) for h in host)
     d2h_bytes = sum(h[3].numel() * 2 for h in host)
-    layer_of = {}
-    for c in stack.chunks:
-        layer_of[id(c)] = c
+    prev = {"done": None, "read_back": [None] * len(stack.chunks)}
 
     def step():
-        # admission + map upload for the step
-        for si, s in enumerate(stack.sessions):
-            s.plan_stack(scores)
-            if stack.persist:
-                s.upload(sp)
-        loaded = []
-        for i, c in enumerate(stack.chunks):
-            hq, hk, hv, _ = host[i]
-            with torch.cuda.stream(h2d):
+        with torch.cuda.stream(h2d):
+            if prev["done"] is not None:
+                h2d.wait_event(prev["done"])      # last step's layers have read map and inputs
+            # admission + map upload for the step, ahead of the bulk copies
+            for s in stack.sessions:
+                s.plan_stack(scores)
+                if stack.persist:
+                    s.upload(hp)
+            map_ready = torch.cuda.Event()
+            map_ready.record(h2d)
+            loaded = []
+            for i, c in enumerate(stack.chunks):
+                hq, hk, hv, _ = host[i]
                 c.k.copy_(hk, non_blocking=True)
                 c.v.copy_(hv, non_blocking=True)
                 c.q.copy_(hq, non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(h2d)
-            loaded.append(ev)
+                loaded.append(ev)
+        stream.wait_event(map_ready)
         for i, c in enumerate(stack.chunks):
             stream.wait_event(loaded[i])
+            if prev["read_back"][i] is not None:
+                stream.wait_event(prev["read_back"][i])
             if stack.persist:
                 stack.sessions[c.session].stage_layer(c.slot, c.k.data_ptr(), c.v.data_ptr(), sp)
             stack.attend(c, sp)
@@ -401,10 +418,12 @@ def run_e2e(args, stack, scores, dev, stream, world, local_rank):
             d2h.wait_event(ev)
             with torch.cuda.stream(d2h):
                 host[i][3].copy_(c.o, non_blocking=True)
+                rb = torch.cuda.Event()
+                rb.record(d2h)
+            prev["read_back"][i] = rb
+        prev["done"] = ev
         if stack.persist and stack.use_window:
             stack.sessions[0].clear_window(sp)
-        stream.wait_stream(d2h)
-        stream.wait_stream(h2d)
 
     for _ in range(max(1, min(args.warmup, 2))):
         step()
@@ -413,10 +432,12 @@ def run_e2e(args, stack, scores, dev, stream, world, local_rank):
         dist.barrier(device_ids=[local_rank])
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    n = max(1, min(args.steps, 3))
+    n = max(1, min(args.steps, 5))
     e0.record(stream)
     for _ in range(n):
         step()
+    stream.wait_stream(d2h)
+    stream.wait_stream(h2d)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / n

@@ -73,6 +73,14 @@ constexpr int kRegsLow = 104;      // registers per thread, warps 0-3 (producers
 constexpr int kRegsHigh = 200;     // registers per thread, warps 4-11 (softmax)
 static_assert(kRegsLow * 128 + 2 * kRegsHigh * 128 <= 65536, "register split exceeds the SM");
 constexpr float kRedoSum = 256.f;  // a tile row sum above this recomputes with the new max
+// Which of the 16 column pairs of each 32-column chunk take the FMA-pipe
+// exponential (ex2_poly2) instead of MUFU: bit p = pair p.  Two pairs in
+// sixteen (one exponential in eight) measured fastest on the 21-frame
+// layer; four, six and eight pairs were 1 %, 9 % and 12 % slower.
+#ifndef KVP_POLY_PAIRS
+#define KVP_POLY_PAIRS 0x8080u
+#endif
+constexpr uint32_t kPolyPairs = KVP_POLY_PAIRS;
 
 struct __align__(1024) Smem {
     uint8_t q[kQTiles][kTileBytes];
@@ -384,7 +392,7 @@ __device__ __forceinline__ float exp_row(uint32_t s_addr, float m, float sl2, in
             }
             float x0, x1, p0, p1;
             f2_unpack(f2_fma(f2_pack(s0, s1), sl2x2, negm2), x0, x1);
-            if ((c & 15) == 14) {   // one pair in eight on the FMA pipe
+            if ((kPolyPairs >> (c >> 1)) & 1u) {   // selected pairs on the FMA pipe
                 ex2_poly2(x0, x1, p0, p1);
             } else {
                 p0 = ex2_approx(x0);
