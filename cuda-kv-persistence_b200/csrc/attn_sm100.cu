@@ -15,11 +15,13 @@
 // 128x128x128 GEMMs.  Warp roles (384 threads):
 //   warp 0      Q loads and the K producer, warp 2 the V producer: each reads
 //               the KVMap for its 128-key tile, classifies every 8-row group
-//               (all base / one ascending arena run / mixed) and stages the
-//               tile with TMA boxes (one 128-row box per panel when the whole
-//               tile is base rows, power-of-two boxes per run otherwise);
-//               mixed groups and padding are copied with 16-byte cp.async
-//               into the same 128B-swizzled layout
+//               (all base / one ascending arena run / all arena in any slot
+//               order / mixed) and stages the tile with TMA: one 128-row box
+//               per panel when the whole tile is base rows, power-of-two
+//               boxes per run otherwise, two four-row TMA gathers per panel
+//               for scattered arena groups; mixed groups and padding are
+//               copied with 16-byte cp.async into the same 128B-swizzled
+//               layout
 //   warp 1      TMEM allocation and the single-thread MMA issuer, in the
 //               order S0_j, PV1_{j-1}, S1_j, PV0_j: while one tile's softmax
 //               runs, the tensor cores work on the other tile.  Each GEMM is
@@ -105,6 +107,7 @@ struct TmaMaps {
     CUtensorMap q8;                 // Q [q_rows][D], box 64 x 8
     CUtensorMap kv[2][kBoxKinds];   // K / V [kv_rows][D], box 64 x (8 << i)
     CUtensorMap a[kBoxKinds];       // arena [arena_rows][2D], box 64 x (8 << i)
+    CUtensorMap a1;                 // arena, box 64 x 1 (TMA gather of scattered slots)
 };
 
 struct Params {
@@ -117,6 +120,7 @@ struct Params {
     long long q_rows, kv_rows, arena_rows;
     int D, T, frames, q_frame0, mode, window, head0, nheads, flat, items_per_head, n_qt, n_pairs;
     int base_boxes, arena_boxes;   // box kinds usable (heights <= tensor rows); 0 = no arena TMA
+    int arena_gather;              // 1 = maps.a1 is encoded (scattered arena groups by TMA gather)
     float scale_log2;
     // Key-range split (per-frame tiling only): splits > 1 writes fp32 partial
     // (O, m, l) to ws instead of bf16 output; combine_splits_kernel merges.
@@ -570,9 +574,16 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             const bool group_pad = even ? pad[0] : p_pad0;
             const bool g_base = all_neg && p_neg && !group_pad;
             const bool g_arena = P.arena_boxes > 0 && asc && p_asc && (even ? p_m0 == m[0] + 4 : m[0] == p_m0 + 4);
+            // Every row of the group in the arena, in any slot order (LIFO slot
+            // reuse leaves descending runs), none of it padding: two TMA
+            // gathers of four rows per panel.
+            const bool all_arena = !pad[3] && m[0] >= 0 && m[1] >= 0 && m[2] >= 0 && m[3] >= 0;
+            const bool p_all_arena = __shfl_xor_sync(0xffffffffu, all_arena, 1);
+            const bool g_gather = P.arena_gather && all_arena && p_all_arena && !g_arena;
             const unsigned base_mask = __ballot_sync(0xffffffffu, g_base);
             const unsigned arena_mask = __ballot_sync(0xffffffffu, g_arena);
-            const unsigned mixed_mask = ~(base_mask | arena_mask);
+            const unsigned gather_mask = __ballot_sync(0xffffffffu, g_gather);
+            const unsigned mixed_mask = ~(base_mask | arena_mask | gather_mask);
             // One 128-row box per panel when no row is remapped; the box
             // starts inside the tensor (r0 < khi <= kv_rows).
             const bool whole_base = __all_sync(0xffffffffu, all_neg) && P.base_boxes == kBoxKinds;
@@ -592,7 +603,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     bytes = kTileBytes;
                 } else {
                     for (int g = 0; g < 16; ++g)
-                        if (((base_mask | arena_mask) >> (2 * g)) & 1u) bytes += 2 * kGroupPanel;
+                        if (((base_mask | arena_mask | gather_mask) >> (2 * g)) & 1u) bytes += 2 * kGroupPanel;
                 }
                 mbar_expect_tx(full, bytes);
                 if (whole_base)
@@ -618,6 +629,16 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                                         col + 64 * p, row, full);
                         off += 1 << kind;
                     }
+                }
+                // Scattered arena groups: each lane of the pair gathers its own
+                // four rows (rows 0-3 of the group from the even lane, 4-7 from
+                // the odd one) into both panels.
+                if (g_gather) {
+                    const int g = lane >> 1;
+                    const uint32_t half = (lane & 1) ? 4u * 128u : 0u;
+                    for (int p = 0; p < 2; ++p)
+                        tma_gather4(dst_tile + p * kPanel + g * kGroupPanel + half, &maps.a1, acol + 64 * p,
+                                    (int)m[0], (int)m[1], (int)m[2], (int)m[3], full);
                 }
                 // Mixed / padding groups: lane -> (panel = lane/16, row = (lane/2)%8,
                 // chunks 4*(lane%2) .. +3); one 16-byte cp.async per chunk into the
@@ -1145,6 +1166,7 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
         if (!rc && arena_boxes)
             rc = make_map(&maps.a[i], io.arena, io.arena_rows, 2 * D, 2 * D, 8u << (i < arena_boxes ? i : 0));
     }
+    if (!rc && arena_boxes) rc = make_map(&maps.a1, io.arena, io.arena_rows, 2 * D, 2 * D, 1);
     if (rc) return rc;
     if (base_boxes == 0 || io.q_rows < 8) {
         set_error("attn_bf16: Q and K/V need at least 8 rows");
@@ -1177,6 +1199,7 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
                               : d.frames * P.n_pairs;
     P.base_boxes = base_boxes;
     P.arena_boxes = arena_boxes;
+    P.arena_gather = arena_boxes > 0 ? 1 : 0;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)kDH);
     P.splits = 1;
     P.ws = nullptr;

@@ -83,6 +83,19 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         ::"r"(smem_u32(dst)), "l"((unsigned long long)map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+// TMA gather: rows y0..y3 (any order, any rows) of a 2D tensor whose map has
+// a one-row box, columns [x, x + box width), into four consecutive rows of
+// shared memory at dst (128-byte aligned; the map's swizzle applies by
+// address, as for a four-row box stored there).
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int x, int y0, int y1,
+                                            int y2, int y3, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        ::"r"(smem_u32(dst)), "l"((unsigned long long)map), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3),
+          "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

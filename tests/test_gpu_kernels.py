@@ -199,6 +199,52 @@ def test_bf16_causal_policies_bitwise(cuda, T):
         assert np.array_equal(results[name], results["none"]), name
 
 
+def _tile_slot_map(F, T, n_tiles, order, seed):
+    """KVMap of whole 16-row admission tiles whose rows sit on arena slots in
+    the given order: "desc" puts each tile on descending slots (what LIFO slot
+    reuse in streaming mode produces), "perm" scatters every row over the
+    arena at random."""
+    rng = np.random.default_rng(seed)
+    tpf = (T + 15) // 16
+    m = np.full(F * T, -1, dtype=np.int64)
+    rows, nxt = [], 0
+    for gid in rng.choice(F * tpf, size=n_tiles, replace=False):
+        f, i = divmod(int(gid), tpf)
+        cnt = min(16, T - 16 * i)
+        r = np.arange(f * T + 16 * i, f * T + 16 * i + cnt)
+        rows.append(r)
+        if order == "desc":
+            m[r] = nxt + cnt - 1 - np.arange(cnt)
+        nxt += cnt
+    if order == "perm":
+        allr = np.concatenate(rows)
+        m[allr] = rng.permutation(len(allr))
+    return m, nxt
+
+
+@pytest.mark.parametrize("T", [300, 1560])
+@pytest.mark.parametrize("flat", [False, True])
+def test_bf16_tile_slots_in_any_order_bitwise(cuda, T, flat):
+    """Admitted tiles on descending or scattered arena slots: 8-row key
+    groups wholly in the arena are fetched by TMA gather (four rows per
+    instruction), groups that mix base and arena rows (frames of 300 tokens
+    start off the 8-row grid) by cp.async.  Outputs bitwise equal to None and
+    within tolerance of the oracle."""
+    from kvp.attention import read_status
+    F, H = 3, 2
+    D, q, k, v = _bf16_case(F, T, H, seed=21)
+    want = attention_frames(q, k, v, frames=F, tokens=T, heads=H, head_dim=128, mode="cross")
+    kw = dict(tokens=T, frames=F, heads=H, mode="causal", flat=flat)
+    read_status()
+    none = _run_bf16(q, k, v, None, None, **kw)
+    check_bf16(none, want, "none")
+    n_tiles = F * ((T + 15) // 16) // 2
+    for order in ("desc", "perm"):
+        m, cap = _tile_slot_map(F, T, n_tiles, order, seed=22)
+        got = _run_bf16(q, k, v, m, build_arena(k, v, m, cap), **kw)
+        assert np.array_equal(got, none), order
+
+
 def test_bf16_flat_stack_matches_per_frame(cuda):
     """Flat query tiling across frame edges (the stack layout) vs the oracle."""
     F, T, H = 4, 300, 2
