@@ -461,6 +461,9 @@ def run_matrix(args) -> int:
                                       streaming=args.streaming):
             print(json.dumps({"metric": "config5 cell", "streaming": args.streaming, **row}),
                   flush=True)
+    elif args.matrix == 10:
+        for row in matrix.run_slot_orders(reps=max(1, args.reps) * 10, seed=args.seed):
+            print(json.dumps({"metric": "one config-4 layer by arena slot order", **row}), flush=True)
     elif args.matrix == 9:
         for row in matrix.run_sdpa_compare(reps=max(1, args.reps), seed=args.seed):
             print(json.dumps({"metric": "intra-frame attention, 12 heads, bf16", **row}), flush=True)
@@ -501,7 +504,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--matrix", type=int, choices=[2, 3, 5, 6, 7, 8, 9], default=0,
+    ap.add_argument("--matrix", type=int, choices=[2, 3, 5, 6, 7, 8, 9, 10], default=0,
                     help="instead of the config-4 line: config 5 (policy x budget x regime, one "
                          "JSON line per cell), config 3 (50 frames x 30 layers, window 5; None "
                          "and ReuseWeighted) or config 2 (one line), per-frame cross attention; "
@@ -511,7 +514,8 @@ def main() -> int:
                          "writing the arena, against cuBLAS + gather); 8: the motion-trace "
                          "producer (GPU optical flow + tile rates) against OpenCV on the host; 9: "
                          "the attention kernel against torch SDPA backends (cuDNN first) on "
-                         "intra-frame attention")
+                         "intra-frame attention; 10: one config-4 layer with admitted tiles on "
+                         "ascending, descending and permuted arena slots against no map")
     ap.add_argument("--reps", type=int, default=3, help="repetitions per cell with --matrix (ABBA)")
     ap.add_argument("--streaming", action="store_true",
                     help="with --matrix 3 or 5: streaming arena (sticky slots, LIFO reuse) instead of "

@@ -586,3 +586,79 @@ def _sdpa_compare_one(*, reps, warmup, frames, tokens, heads, seed, device):
         except Exception as e:  # backend not available for this device / layout
             res.append({"leg": f"sdpa {name}", "unavailable": str(e).splitlines()[0][:160]})
     return res
+
+
+def slot_order_map(rows_total: int, tile_tokens: int, n_tiles: int, order: str, *, seed: int,
+                   device="cuda"):
+    """KVMap + arena slots for `n_tiles` admitted tiles (every other
+    `tile_tokens`-row tile from row 0) in one of three slot orders:
+    "ascending" (each tile on consecutive rising slots, what arena mode
+    produces), "descending" (each tile on falling slots, what LIFO slot reuse
+    in streaming mode produces) or "permuted" (every row on a random slot).
+    Returns (kvmap int64 [rows_total], admitted rows, their slots)."""
+    tiles = torch.arange(0, rows_total // tile_tokens, 2, device=device)[:n_tiles]
+    rows = (tiles[:, None] * tile_tokens + torch.arange(tile_tokens, device=device)).reshape(-1)
+    base = torch.arange(rows.numel(), device=device).view(-1, tile_tokens)
+    if order == "ascending":
+        slots = base
+    elif order == "descending":
+        slots = base.flip(1)
+    elif order == "permuted":
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        slots = torch.randperm(rows.numel(), generator=g).to(device)
+    else:
+        raise ValueError(order)
+    slots = slots.reshape(-1)
+    kvmap = torch.full((rows_total,), -1, dtype=torch.int64, device=device)
+    kvmap[rows] = slots
+    return kvmap, rows, slots
+
+
+def run_slot_orders(*, reps: int = 40, warmup: int = 3, frames: int = 21, tokens: int = 1560,
+                    heads: int = 12, admitted_tiles: int = 640, seed: int = 0,
+                    device="cuda") -> list[dict]:
+    """One config-4 layer (flat causal tiles, 21 frames x 1560 tokens, 12
+    heads) with `admitted_tiles` 16-row tiles (10,240 of 32,760 key rows at
+    the default) held in the arena in each slot order of `slot_order_map`,
+    against the same launch without a map.  The producer fetches ascending
+    runs with TMA boxes and scattered all-arena 8-row groups with TMA gathers;
+    every output must be bitwise equal to the unmapped launch's."""
+    R, D = frames * tokens, heads * 128
+    q, k, v = qkv(R, D, seed=seed, device=device)
+    out = torch.empty_like(q)
+    flop = sum(4.0 * tokens * (f + 1) * tokens * 128 for f in range(frames)) * heads
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    legs = {"none": (None, None, 0)}
+    for order in ("ascending", "descending", "permuted"):
+        kvmap, rows, slots = slot_order_map(R, 16, admitted_tiles, order, seed=seed + 1, device=device)
+        arena = torch.empty(rows.numel(), 2 * D, dtype=torch.bfloat16, device=device)
+        arena[slots, :D] = k[rows]
+        arena[slots, D:] = v[rows]
+        legs[order] = (kvmap, arena, rows.numel())
+
+    def launch(leg):
+        kvmap, arena, arows = legs[leg]
+        attn_bf16(q, k, v, out, tokens=tokens, frames=frames, heads=heads, mode="causal", flat=True,
+                  kvmap=kvmap, arena=arena, arena_rows=arows, stream=stream)
+
+    read_status()
+    launch("none")
+    torch.cuda.synchronize()
+    ref = out.clone()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    res = []
+    for leg in legs:
+        for _ in range(warmup):
+            launch(leg)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            launch(leg)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res.append({"slots": leg, "arena_rows": legs[leg][2], "ms": round(ms, 4),
+                    "tflops": round(flop / (ms / 1e3) / 1e12, 1),
+                    "bitwise_eq_none": bool(torch.equal(out, ref)), "device_status": read_status()})
+    return res

@@ -33,3 +33,25 @@ def test_config3_flops():
     # 50 frames, window of 5 frames: 240 frame-units per (layer, head); 1.0765e14 FLOP
     assert matrix.window_flops(50, 1560, 12, 30, 5) == pytest.approx(1.0765e14, rel=1e-4)
     assert matrix.window_flops(3, 1560, 12, 1, 5) == pytest.approx(matrix.cross_flops(3, 1560, 12))
+
+
+@pytest.mark.parametrize("order", ["ascending", "descending", "permuted"])
+def test_slot_order_maps(order):
+    """--matrix 10 maps: whole 16-row tiles, every slot used once; ascending
+    and descending runs inside each tile as named."""
+    import torch
+    from kvp.matrix import slot_order_map
+    m, rows, slots = slot_order_map(32760, 16, 640, order, seed=1, device="cpu")
+    assert rows.numel() == 10240 and int((m >= 0).sum()) == 10240
+    assert sorted(slots.tolist()) == list(range(10240))
+    assert bool((rows % 32 < 16).all())                     # every other tile
+    per_tile = m[rows].view(-1, 16)
+    d = per_tile[:, 1:] - per_tile[:, :-1]
+    if order == "ascending":
+        assert bool((d == 1).all())
+    elif order == "descending":
+        assert bool((d == -1).all())
+    else:
+        assert not bool((d == 1).all()) and not bool((d == -1).all())
+    with pytest.raises(ValueError):
+        slot_order_map(64, 16, 1, "sideways", seed=0, device="cpu")
