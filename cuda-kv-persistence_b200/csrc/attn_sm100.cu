@@ -1125,13 +1125,11 @@ int make_bf16_tensor_map(CUtensorMap* m, const void* base, long long rows, long 
     return make_map(m, base, rows, cols, pitch, box_rows);
 }
 
-int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
-                     bool allow_split) {
+int check_attn_bf16(const LayerIO& io, const AttnDesc& d) {
     const long long T = d.tokens;
-    const int D = d.heads * kDH;
     if (d.head_dim != kDH || d.heads <= 0 || T <= 0 || d.frames <= 0 || d.q_frame0 < 0 ||
         d.nheads <= 0 || d.head0 < 0 || d.head0 + d.nheads > d.heads || d.window < 0 ||
-        (d.mode != 0 && d.mode != 1) || !io.q || !io.k || !io.v || !io.out || !d_status) {
+        (d.mode != 0 && d.mode != 1) || !io.q || !io.k || !io.v || !io.out) {
         set_error("attn_bf16: bad descriptor (head_dim must be %d)", kDH);
         return KVP_ERR_ARG;
     }
@@ -1148,6 +1146,19 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
     if (((uintptr_t)io.q | (uintptr_t)io.k | (uintptr_t)io.v | (uintptr_t)io.out |
          (uintptr_t)io.arena) & 15) {
         set_error("attn_bf16: Q/K/V/Out/Arena must be 16-byte aligned");
+        return KVP_ERR_ARG;
+    }
+    return KVP_OK;
+}
+
+int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
+                     bool allow_split) {
+    const long long T = d.tokens;
+    const int D = d.heads * kDH;
+    const int rc_check = check_attn_bf16(io, d);
+    if (rc_check != KVP_OK) return rc_check;
+    if (!d_status) {
+        set_error("attn_bf16: no status word");
         return KVP_ERR_ARG;
     }
     TmaMaps maps;

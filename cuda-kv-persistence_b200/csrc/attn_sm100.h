@@ -51,6 +51,10 @@ struct AttnDesc {
 int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
                      bool allow_split = true);
 
+// The launcher's argument checks alone (descriptor, row coverage, 16-byte
+// alignment), touching no device state: KVP_OK or KVP_ERR_ARG with a message.
+int check_attn_bf16(const LayerIO& io, const AttnDesc& d);
+
 // 2D TMA map of a bf16 row-major tensor [rows][cols] (row pitch `pitch`
 // elements), box 64 columns x box_rows rows, 128B swizzle.  Encoded maps are
 // cached by (base, shape, pitch, box).

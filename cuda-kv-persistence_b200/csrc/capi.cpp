@@ -518,13 +518,16 @@ KVP_API int kvp_probe_bounded_wait(long long limit_ns, void* stream) {
 
 KVP_API int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream) {
     if (!io || !d) return kvp::KVP_ERR_ARG;
-    int rc = kvp::flush_all_managers();
-    if (rc != kvp::KVP_OK) return rc;
-    int* st = kvp::status_word();
-    if (!st) return kvp::KVP_ERR_CUDA;
     kvp::LayerIO L{io->q, io->k, io->v, io->out, io->arena, io->kvmap,
                    io->q_rows, io->kv_rows, io->arena_rows};
     kvp::AttnDesc A{d->tokens, d->frames, d->q_frame0, d->mode, d->window,
                     d->heads, d->head_dim, d->head0, d->nheads, d->flat};
+    // Bad arguments are reported before any device state is touched.
+    int rc = kvp::check_attn_bf16(L, A);
+    if (rc != kvp::KVP_OK) return rc;
+    rc = kvp::flush_all_managers();
+    if (rc != kvp::KVP_OK) return rc;
+    int* st = kvp::status_word();
+    if (!st) return kvp::KVP_ERR_CUDA;
     return kvp::launch_attn_bf16(L, A, st, (cudaStream_t)stream);
 }

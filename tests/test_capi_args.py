@@ -90,3 +90,69 @@ def test_session_produce_preconditions_without_device_buffers():
     assert rc == ERR_ARG
     assert b"produce" in lib().kvp_last_error()
     s.close()
+
+
+# ---------------------------------------------------------------- attention
+ERR_CUDA = -2
+
+
+def _attn(io_kw=None, **d_kw):
+    """kvp_attn_bf16 on fake, aligned addresses: a 2-frame causal launch of
+    2 heads over 300-token frames unless overridden."""
+    from kvp._lib import AttnDesc, LayerIO
+    io = dict(q=0x10000, k=0x20000, v=0x30000, out=0x40000, arena=0, kvmap=0, q_rows=600,
+              kv_rows=600, arena_rows=0)
+    io.update(io_kw or {})
+    d = dict(tokens=300, frames=2, q_frame0=0, mode=1, window=0, heads=2, head_dim=128, head0=0,
+             nheads=2, flat=0)
+    d.update(d_kw)
+    lio = LayerIO(*(io[k] for k in ("q", "k", "v", "out", "arena", "kvmap", "q_rows", "kv_rows",
+                                    "arena_rows")))
+    ld = AttnDesc(*(d[k] for k in ("tokens", "frames", "q_frame0", "mode", "window", "heads",
+                                   "head_dim", "head0", "nheads", "flat")))
+    return lib().kvp_attn_bf16(C.byref(lio), C.byref(ld), None)
+
+
+@pytest.mark.parametrize("io_kw,d_kw", [
+    (None, dict(head_dim=64)),                       # the kernel is built for 128
+    (None, dict(heads=0, nheads=0)),
+    (None, dict(tokens=0)),
+    (None, dict(frames=0)),
+    (None, dict(q_frame0=-1)),
+    (None, dict(head0=1)),                           # heads [1, 3) of 2
+    (None, dict(nheads=0)),
+    (None, dict(window=-1)),
+    (None, dict(mode=2)),
+    (None, dict(flat=1, mode=0)),                    # flat tiles are causal only
+    (None, dict(flat=1, window=2)),
+    (None, dict(flat=1, tokens=100, frames=6)),      # flat needs >= 128 tokens per frame
+    (None, dict(q_frame0=1)),                        # frames 1..2 need 900 rows
+    (dict(kv_rows=599), {}),
+    (dict(kvmap=0x50000, arena=0x60000, arena_rows=0), {}),   # a map into an empty arena
+    (dict(q=0), {}),
+    (dict(out=0), {}),
+    (dict(k=0x20008), {}),                           # not 16-byte aligned
+    (dict(arena=0x60004, arena_rows=64), {}),
+])
+def test_attn_bf16_rejects_before_touching_the_device(io_kw, d_kw):
+    """Bad descriptors come back as KVP_ERR_ARG with a message, before the
+    entry point flushes queued copies or fetches its device status word."""
+    assert _attn(io_kw, **d_kw) == ERR_ARG
+    assert b"attn_bf16" in lib().kvp_last_error()
+
+
+@pytest.mark.parametrize("io_kw,d_kw", [
+    (None, {}),
+    (None, dict(mode=0)),
+    (None, dict(flat=1)),
+    (None, dict(head0=1, nheads=1, window=2)),
+    (dict(kvmap=0x50000, arena=0x60000, arena_rows=64), {}),
+])
+def test_attn_bf16_valid_descriptors_pass_the_checks(io_kw, d_kw):
+    """Descriptors of the shapes the GPU tests launch get past the argument
+    checks: without a GPU the call then fails on its first CUDA call (the
+    status word), never with KVP_ERR_ARG."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("would launch the kernel on fake addresses")
+    assert _attn(io_kw, **d_kw) == ERR_CUDA
