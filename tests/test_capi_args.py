@@ -9,7 +9,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
-from kvp._lib import MotionParams, QkvIO, lib
+from kvp._lib import AttnDesc, LayerIO, MotionParams, QkvIO, lib
 
 ERR_ARG = -1
 
@@ -99,7 +99,6 @@ ERR_CUDA = -2
 def _attn(io_kw=None, **d_kw):
     """kvp_attn_bf16 on fake, aligned addresses: a 2-frame causal launch of
     2 heads over 300-token frames unless overridden."""
-    from kvp._lib import AttnDesc, LayerIO
     io = dict(q=0x10000, k=0x20000, v=0x30000, out=0x40000, arena=0, kvmap=0, q_rows=600,
               kv_rows=600, arena_rows=0)
     io.update(io_kw or {})
