@@ -84,8 +84,16 @@ KVP_API int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d
                        map_rows, kMaxMapRows);
         return kvp::KVP_ERR_CAPACITY;
     }
+    kvp::AttnDesc A{d->tokens, d->frames, d->q_frame0, d->mode, d->window,
+                    d->heads, d->head_dim, d->head0, d->nheads, d->flat};
+    // Bad arguments are reported before the scratch is looked up or written
+    // (the map pointer only has to be non-null here; it becomes the scratch).
+    kvp::LayerIO L{io->q, io->k, io->v, io->out, io->arena, host_kvmap,
+                   io->q_rows, io->kv_rows, io->arena_rows};
+    int rc = kvp::check_attn_bf16(L, A);
+    if (rc != kvp::KVP_OK) return rc;
     long long* scratch = nullptr;
-    int rc = scratch_for_current_device(&scratch);
+    rc = scratch_for_current_device(&scratch);
     if (rc != kvp::KVP_OK) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     int* status = reinterpret_cast<int*>(scratch);
@@ -94,10 +102,7 @@ KVP_API int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d
     if (host_kvmap)
         KVP_CUDA(cudaMemcpyAsync(dmap, host_kvmap, (size_t)map_rows * sizeof(long long),
                                  cudaMemcpyHostToDevice, s));
-    kvp::LayerIO L{io->q, io->k, io->v, io->out, io->arena, host_kvmap ? dmap : nullptr,
-                   io->q_rows, io->kv_rows, io->arena_rows};
-    kvp::AttnDesc A{d->tokens, d->frames, d->q_frame0, d->mode, d->window,
-                    d->heads, d->head_dim, d->head0, d->nheads, d->flat};
+    L.kvmap = host_kvmap ? dmap : nullptr;
     rc = kvp::launch_attn_bf16(L, A, status, s, /*allow_split=*/false);
     if (rc != kvp::KVP_OK) return rc;
     if (host_status) {

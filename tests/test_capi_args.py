@@ -155,3 +155,21 @@ def test_attn_bf16_valid_descriptors_pass_the_checks(io_kw, d_kw):
     if torch.cuda.is_available():
         pytest.skip("would launch the kernel on fake addresses")
     assert _attn(io_kw, **d_kw) == ERR_CUDA
+
+
+def test_attn_bf16_noalloc_rejects_before_touching_the_device():
+    """The no-alloc entry point refuses a bad descriptor (and a map passed in
+    device memory) before it looks up or writes its static scratch."""
+    io = LayerIO(0x10000, 0x20000, 0x30000, 0x40000, 0, 0, 600, 600, 0)
+    hmap = np.full(600, -1, dtype=np.int64)
+    for d in (AttnDesc(300, 2, 0, 1, 0, 2, 64, 0, 2, 0),      # head_dim 64
+              AttnDesc(300, 3, 0, 1, 0, 2, 128, 0, 2, 0)):    # 900 rows of 600
+        rc = lib().kvp_attn_bf16_noalloc(C.byref(io), C.byref(d),
+                                         hmap.ctypes.data_as(C.c_void_p), None, None)
+        assert rc == ERR_ARG
+        assert b"attn_bf16" in lib().kvp_last_error()
+    io_dev_map = LayerIO(0x10000, 0x20000, 0x30000, 0x40000, 0, 0x50000, 600, 600, 0)
+    rc = lib().kvp_attn_bf16_noalloc(C.byref(io_dev_map), C.byref(AttnDesc(300, 2, 0, 1, 0, 2, 128,
+                                                                          0, 2, 0)),
+                                     None, None, None)
+    assert rc == ERR_ARG
