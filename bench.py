@@ -21,8 +21,9 @@ Printed JSON keys follow the driver contract; `value` times device-resident
 inputs, `e2e` times the same work through the public API with host buffers
 (pinned H2D of Q/K/V and D2H of O every step, pipelined per layer chunk).
 `--impl reference` times the reference's CPU path (the golden attention of
-traces/gen_golden.py, here the oracle's numpy port) on all host threads over
-a bounded sample of the same workload.
+traces/gen_golden.py, restated with the same torch calls in
+oracle/golden_torch.py) on all host threads, set explicitly, over a bounded
+sample of the same workload.
 """
 
 from __future__ import annotations
@@ -123,42 +124,42 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ CPU arms
 def cpu_attention_sample(seconds: float = 12.0, max_heads: int = HEADS, seed: int = 0):
-    """Oracle port of the reference golden (numpy, all host threads) on whole
-    (layer 0, head h) pairs of the stack, heads taken until `seconds` pass."""
-    import numpy as np
+    """The reference's CPU path -- the golden attention of traces/gen_golden.py,
+    restated with the same torch calls (oracle/golden_torch.py) -- on whole
+    (layer 0, head h) pairs of the stack, heads taken until `seconds` pass.
+    Returns (TFLOP/s, pairs done, seconds, threads)."""
     import torch
-    from oracle.attention import attention_frames
+    from oracle import golden_torch
+    threads = golden_torch.set_threads()
     rows = FRAMES * TOKENS
     done_flops, t_total, heads_done = 0.0, 0.0, 0
     per_pair = stack_flops(pairs=1)
     for h in range(max_heads):
         g = torch.Generator().manual_seed(seed * 1_000_003 + h)
         s = HEAD_DIM ** -0.5
-        q, k, v = ((torch.randn(rows, HEAD_DIM, generator=g) * s).to(torch.bfloat16).float().numpy()
+        q, k, v = ((torch.randn(rows, HEAD_DIM, generator=g) * s).to(torch.bfloat16).float()
                    for _ in range(3))
         t0 = time.perf_counter()
-        attention_frames(q, k, v, frames=FRAMES, tokens=TOKENS, heads=1, head_dim=HEAD_DIM,
-                         mode="cross")
+        golden_torch.attention_frames(q, k, v, frames=FRAMES, tokens=TOKENS, heads=1,
+                                      head_dim=HEAD_DIM)
         t_total += time.perf_counter() - t0
         done_flops += per_pair
         heads_done += 1
         if t_total >= seconds:
             break
-    return done_flops / t_total / 1e12, heads_done, t_total
+    return done_flops / t_total / 1e12, heads_done, t_total, threads
 
 
 def run_reference(args, rank: int, world: int) -> int:
     if rank != 0:
         return 0
-    import numpy as np  # noqa: F401
-    cores = os.cpu_count() or 1
     # One step = one whole (layer, head) pair, all 21 query frames.
     for _ in range(args.warmup):
         cpu_attention_sample(seconds=0.0, max_heads=1)
-    t_steps = []
+    t_steps, cores = [], 1
     for i in range(args.steps):
         t0 = time.perf_counter()
-        cpu_attention_sample(seconds=0.0, max_heads=1, seed=i)
+        _, _, _, cores = cpu_attention_sample(seconds=0.0, max_heads=1, seed=i)
         t_steps.append(time.perf_counter() - t0)
     per = stack_flops(pairs=1)
     ms = 1e3 * sum(t_steps) / len(t_steps)
@@ -173,7 +174,8 @@ def run_reference(args, rank: int, world: int) -> int:
                    "head_dim": HEAD_DIM, "sample": "one (layer, head) pair, 21 query frames"},
         "cpu_baseline": {"value": round(val, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": "one (layer, head) pair per step, 21 query frames, "
-                                   "traces/gen_golden.py attention_reference_cross math (numpy)"},
+                                   "traces/gen_golden.py attention_reference_cross restated "
+                                   "with its torch calls (oracle/golden_torch.py), fp32"},
         "e2e": {"value": round(val, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -322,11 +324,12 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
                     "avg_launch_ms": round(attn_ms / max(n_attn, 1), 4)}
         cpu = None
         if world == 1 and not args.no_cpu:
-            tf, heads_done, secs = cpu_attention_sample(seconds=args.cpu_seconds)
-            cpu = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count() or 1,
+            tf, heads_done, secs, threads = cpu_attention_sample(seconds=args.cpu_seconds)
+            cpu = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": threads,
                    "kind": "port",
                    "sample": f"layer 0, {heads_done} head(s) x 21 query frames ({secs:.1f} s), "
-                             "traces/gen_golden.py math in numpy fp32"}
+                             "traces/gen_golden.py attention_reference_cross restated with its "
+                             "torch calls (oracle/golden_torch.py), fp32"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),

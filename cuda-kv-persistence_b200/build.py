@@ -43,7 +43,8 @@ def _deps_newer(obj: Path, src: Path) -> bool:
     t = obj.stat().st_mtime
     if src.stat().st_mtime > t:
         return True
-    return any(h.stat().st_mtime > t for h in CSRC.glob("*.h"))
+    headers = list(CSRC.glob("*.h")) + list((HERE.parent / "include").rglob("*.h"))
+    return any(h.stat().st_mtime > t for h in headers)
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:

@@ -28,7 +28,13 @@
 //     work overlaps on the GPU (different streams, no ordering between them)
 //     race on it;
 //   * it does not issue copies queued by kvtm_* staging calls: call
-//     kvtm_flush (or a window call) first.
+//     kvtm_flush (or a window call) first;
+//   * without host_status the call returns before the map copy has run: a
+//     map in pinned host memory must stay unchanged until `stream` has
+//     passed the call (a map in pageable memory is staged before return);
+//   * the device address of the array is looked up once per device in the
+//     primary context: do not use the entry point from another context on
+//     that device, or after cudaDeviceReset.
 // No cudaMalloc, cudaFree or allocating library routine is called here.
 #include <mutex>
 
@@ -78,20 +84,22 @@ KVP_API int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d
         kvp::set_error("noalloc: pass the KVMap in host memory (host_kvmap), not io->kvmap");
         return kvp::KVP_ERR_ARG;
     }
-    const long long map_rows = (long long)(d->q_frame0 + d->frames) * d->tokens;
+    kvp::AttnDesc A{d->tokens, d->frames, d->q_frame0, d->mode, d->window,
+                    d->heads, d->head_dim, d->head0, d->nheads, d->flat};
+    // Bad arguments are reported before the scratch is looked up or written
+    // (the map pointer only has to be non-null here; it becomes the scratch).
+    // The descriptor is checked first, so a bad descriptor is -1 whatever
+    // the map; only a valid one can be refused for its map size (-3).
+    kvp::LayerIO L{io->q, io->k, io->v, io->out, io->arena, host_kvmap,
+                   io->q_rows, io->kv_rows, io->arena_rows};
+    int rc = kvp::check_attn_bf16(L, A);
+    if (rc != kvp::KVP_OK) return rc;
+    const long long map_rows = ((long long)d->q_frame0 + d->frames) * (long long)d->tokens;
     if (host_kvmap && (map_rows <= 0 || map_rows > kMaxMapRows)) {
         kvp::set_error("noalloc: KVMap of %lld rows exceeds the %lld-row static scratch",
                        map_rows, kMaxMapRows);
         return kvp::KVP_ERR_CAPACITY;
     }
-    kvp::AttnDesc A{d->tokens, d->frames, d->q_frame0, d->mode, d->window,
-                    d->heads, d->head_dim, d->head0, d->nheads, d->flat};
-    // Bad arguments are reported before the scratch is looked up or written
-    // (the map pointer only has to be non-null here; it becomes the scratch).
-    kvp::LayerIO L{io->q, io->k, io->v, io->out, io->arena, host_kvmap,
-                   io->q_rows, io->kv_rows, io->arena_rows};
-    int rc = kvp::check_attn_bf16(L, A);
-    if (rc != kvp::KVP_OK) return rc;
     long long* scratch = nullptr;
     rc = scratch_for_current_device(&scratch);
     if (rc != kvp::KVP_OK) return rc;

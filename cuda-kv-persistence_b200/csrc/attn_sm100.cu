@@ -1137,7 +1137,7 @@ int check_attn_bf16(const LayerIO& io, const AttnDesc& d) {
         set_error("attn_bf16: flat query tiles need causal mode, no window and tokens >= %d", kBM);
         return KVP_ERR_ARG;
     }
-    const long long q_end = (long long)(d.q_frame0 + d.frames) * T;
+    const long long q_end = ((long long)d.q_frame0 + d.frames) * T;
     if (io.q_rows < q_end || io.kv_rows < q_end || (io.kvmap && io.arena && io.arena_rows <= 0)) {
         set_error("attn_bf16: q_rows/kv_rows (%lld/%lld) do not cover frames up to row %lld",
                   io.q_rows, io.kv_rows, q_end);

@@ -173,35 +173,54 @@ KVP_API long kvtm_window_log(void* m, long* bytes_out, int* prop_out, long cap) 
 KVP_API long kvtm_reset_calls(void* m) { return static_cast<KVTileManager*>(m)->reset_calls(); }
 
 // ============================================================ attn_forward_*
-// Reference entry points src/attn_kernel.h:15-29 (C linkage here).
+// Reference entry points src/attn_kernel.h:15-29, C linkage here; the C++
+// linkage pair the reference's own header declares is in cxx_abi.cpp.  Both
+// forward to kvp::fp32_launcher / kvp::fp32_single_frame.
+
+namespace kvp {
+
+void fp32_launcher(const float* d_q, const float* d_k, const float* d_v, const float* d_arena,
+                   const long* d_kvmap, float* d_out, int frames, int T, int D, int heads,
+                   bool remap) {
+    flush_all_managers();
+    int* st = status_word();
+    if (remap) {
+        // Per-frame intra launches with per-frame map slices (legacy path).
+        for (int f = 0; f < frames; ++f)
+            launch_attn_fp32(d_q + (size_t)f * T * D, d_k + (size_t)f * T * D,
+                             d_v + (size_t)f * T * D, d_arena,
+                             d_kvmap ? (const int64_t*)d_kvmap + (size_t)f * T : nullptr,
+                             d_out + (size_t)f * T * D, T, D, heads, 0, T, INT64_MAX, 1, 0, st,
+                             0);
+    } else {
+        launch_attn_fp32(d_q, d_k, d_v, nullptr, nullptr, d_out, T, D, heads, 0, T, 0, frames,
+                         T, st, 0);
+    }
+}
+
+void fp32_single_frame(const float* d_q_f, const float* d_k, const float* d_v,
+                       const float* d_arena, const long* d_kvmap_f, float* d_out_f, int T, int D,
+                       int heads, int cross, int frame_idx) {
+    flush_all_managers();
+    const int64_t span = cross ? (int64_t)(frame_idx + 1) * T : (int64_t)T;
+    launch_attn_fp32(d_q_f, d_k, d_v, d_arena, (const int64_t*)d_kvmap_f, d_out_f, T, D, heads,
+                     0, span, INT64_MAX, 1, 0, status_word(), 0);
+}
+
+}  // namespace kvp
 
 KVP_API void attn_forward_launcher(const float* d_q, const float* d_k, const float* d_v,
                                    const float* d_arena, const long* d_kvmap, float* d_out,
                                    int frames, int T, int D, int heads, bool remap) {
-    kvp::flush_all_managers();
-    int* st = kvp::status_word();
-    if (remap) {
-        // Per-frame intra launches with per-frame map slices (legacy path).
-        for (int f = 0; f < frames; ++f)
-            kvp::launch_attn_fp32(d_q + (size_t)f * T * D, d_k + (size_t)f * T * D,
-                                  d_v + (size_t)f * T * D, d_arena,
-                                  d_kvmap ? (const int64_t*)d_kvmap + (size_t)f * T : nullptr,
-                                  d_out + (size_t)f * T * D, T, D, heads, 0, T, INT64_MAX, 1, 0,
-                                  st, 0);
-    } else {
-        kvp::launch_attn_fp32(d_q, d_k, d_v, nullptr, nullptr, d_out, T, D, heads, 0, T, 0,
-                              frames, T, st, 0);
-    }
+    kvp::fp32_launcher(d_q, d_k, d_v, d_arena, d_kvmap, d_out, frames, T, D, heads, remap);
 }
 
 KVP_API void attn_forward_single_frame(const float* d_q_f, const float* d_k, const float* d_v,
                                        const float* d_arena, const long* d_kvmap_f,
                                        float* d_out_f, int T, int D, int heads, int cross,
                                        int frame_idx) {
-    kvp::flush_all_managers();
-    const int64_t span = cross ? (int64_t)(frame_idx + 1) * T : (int64_t)T;
-    kvp::launch_attn_fp32(d_q_f, d_k, d_v, d_arena, (const int64_t*)d_kvmap_f, d_out_f, T, D,
-                          heads, 0, span, INT64_MAX, 1, 0, kvp::status_word(), 0);
+    kvp::fp32_single_frame(d_q_f, d_k, d_v, d_arena, d_kvmap_f, d_out_f, T, D, heads, cross,
+                           frame_idx);
 }
 
 // ===================================================================== kvp_*

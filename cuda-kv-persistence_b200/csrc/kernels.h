@@ -43,4 +43,15 @@ int launch_attn_fp32(const float* q, const float* k, const float* v, const float
                      int64_t k_hi, int64_t arena_rows, int frames, int64_t frame_stride_rows,
                      int* d_status, cudaStream_t stream);
 
+// The reference's two fp32 entry points (src/attn_kernel.h:15-29): flush
+// every manager's queued staging copies, then launch on the legacy default
+// stream.  Exported twice, with C linkage (capi.cpp) and with the C++
+// linkage of the reference's header (cxx_abi.cpp).
+void fp32_launcher(const float* d_q, const float* d_k, const float* d_v, const float* d_arena,
+                   const long* d_kvmap, float* d_out, int frames, int T, int D, int heads,
+                   bool remap);
+void fp32_single_frame(const float* d_q_f, const float* d_k, const float* d_v,
+                       const float* d_arena, const long* d_kvmap_f, float* d_out_f, int T, int D,
+                       int heads, int cross, int frame_idx);
+
 }  // namespace kvp

@@ -25,11 +25,17 @@
 
 #include <cuda_runtime.h>
 
+// Global, as in the reference (src/kv_tile_manager.h:15-19); the C++ drop-in
+// header include/cxx/kv_tile_manager.h declares the same enum under the same
+// guard.
+#ifndef KVP_KVTM_RESULT_DECLARED
+#define KVP_KVTM_RESULT_DECLARED
 enum KvtmResult {
     KVTM_ADMITTED = 1,
     KVTM_REFUSED_BUDGET = 0,
     KVTM_INVALID = -1,  // bad args, duplicate admit, or window larger than allowed
 };
+#endif
 
 namespace kvp {
 
@@ -96,6 +102,8 @@ public:
     size_t arena_window_span() const;
     size_t streaming_window_span() const;
     long slot_high_water() const { return slot_high_water_; }
+    size_t arena_next_row() const { return arena_next_row_; }
+    bool initialized() const { return initialized_; }
     size_t arena_capacity() const { return arena_cap_; }
     size_t row_stride_bytes() const { return arena_row_stride_floats_ * sizeof(float); }
 

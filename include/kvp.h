@@ -109,8 +109,15 @@ int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
  * any stream capture); all calls share the array (the status word is reset
  * per call), so calls that overlap on the GPU race.  host_status (may be
  * NULL) receives the status word and then the call synchronises `stream`.
- * Queued kvtm_* staging copies are not flushed: call kvtm_flush first.
- * Returns -3 when the map exceeds the limit. */
+ * Without host_status the call returns before the map copy has run: a map
+ * in pinned host memory must stay unchanged until `stream` has passed this
+ * call (synchronise the stream or an event recorded after it before
+ * refilling the buffer); a map in pageable memory is staged before return.
+ * The array's device address is looked up once per device in the primary
+ * context: do not call this from another context on that device, or after
+ * cudaDeviceReset.  Queued kvtm_* staging copies are not flushed: call
+ * kvtm_flush first.  Returns -1 for a bad descriptor (checked first), -3
+ * when a valid descriptor's map exceeds the limit. */
 int kvp_attn_bf16_noalloc(const kvp_layer_io* io, const kvp_attn_desc* d,
                           const long long* host_kvmap, int* host_status, void* stream);
 

@@ -70,7 +70,7 @@ extern "C" int kvpref_run_window(int policy, int streaming, int window, int fram
         std::vector<char> selected((size_t)((f + 1) * num_tiles), 0);
         std::vector<long> gids;
         for (int i = 0; i < count; ++i) {
-            if (ids[i] < 0 || ids[i] >= n_cand) continue;  // see DESIGN: uniform overflow
+            if (ids[i] < 0 || ids[i] >= n_cand) continue;  // Uniform may name ids past the candidates: nothing to stage
             const long gid = base * num_tiles + ids[i];
             selected[(size_t)gid] = 1;
             gids.push_back(gid);

@@ -1,6 +1,8 @@
 """Regenerates the committed golden fixtures from the reference's own code.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--only reuse|qkv|motion]
+    python tests/golden/make_golden.py --ref <reference checkout> [--only reuse|qkv|motion|cxx]
+
+(--ref defaults to $KVP_REF_ROOT.)
 
 Needs the reference sources (read, never copied) and is run once, on a host
 where they exist; the tests only read the files it writes:
@@ -38,14 +40,20 @@ where they exist; the tests only read the files it writes:
                           traces/gen_motion_from_video.py (OpenCV Farneback)
                           run on a seeded synthetic clip: per-tile change
                           rates, is_static and reuse, tau.  ``--only motion``.
+* ``cxx_layout_ref.json`` sizes, member offsets and enum values of the
+                          reference's C++ classes as a caller compiled
+                          against its headers sees them
+                          (``cxx_layout_probe.cpp``).  ``--only cxx``.
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import importlib.util
 import json
+import subprocess
 import sys
 import tempfile
 from pathlib import Path
@@ -231,12 +239,31 @@ def motion_fixture(ref: Path):
         shutil.rmtree(work, ignore_errors=True)
 
 
+def cxx_layout_fixture(ref: Path):
+    """cxx_layout_ref.json: the object layout (sizes, member offsets, enum
+    values) that a caller compiled against the reference's own C++ headers
+    (src/kv_tile_manager.h, src/tile_gating_policy.h) allocates.
+    tests/test_cxx_boundary.py compiles the same probe against include/cxx/
+    and requires the same numbers."""
+    with tempfile.TemporaryDirectory() as td:
+        exe = Path(td) / "probe"
+        subprocess.run(["g++", "-std=c++17", "-I", str(ref / "src"), str(HERE / "cxx_layout_probe.cpp"),
+                        "-o", str(exe)], check=True)
+        out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    layout = json.loads(out)
+    layout["generator"] = "tests/golden/make_golden.py --only cxx (probe built against the reference's src/*.h)"
+    (HERE / "cxx_layout_ref.json").write_text(json.dumps(layout, indent=1) + "\n")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--only", choices=("reuse", "qkv", "motion"), default=None,
+    ap.add_argument("--ref", default=os.environ.get("KVP_REF_ROOT"),
+                    help="root of a GauthamMK-0/cuda-kv-persistence checkout (default: $KVP_REF_ROOT)")
+    ap.add_argument("--only", choices=("reuse", "qkv", "motion", "cxx"), default=None,
                     help="regenerate one fixture set only")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set KVP_REF_ROOT to the reference checkout")
     ref = Path(args.ref)
     orc.build(str(ref))
     if args.only == "reuse":
@@ -247,6 +274,9 @@ def main():
         return
     if args.only == "motion":
         motion_fixture(ref)
+        return
+    if args.only == "cxx":
+        cxx_layout_fixture(ref)
         return
     from kvp import traces
 

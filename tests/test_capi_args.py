@@ -168,6 +168,14 @@ def test_attn_bf16_noalloc_rejects_before_touching_the_device():
                                          hmap.ctypes.data_as(C.c_void_p), None, None)
         assert rc == ERR_ARG
         assert b"attn_bf16" in lib().kvp_last_error()
+    # a bad descriptor with a host map is -1, not a capacity refusal
+    for d in (AttnDesc(0, 2, 0, 1, 0, 2, 128, 0, 2, 0),        # tokens 0
+              AttnDesc(300, 0, 0, 1, 0, 2, 128, 0, 2, 0),      # frames 0
+              AttnDesc(300, 2, -5, 1, 0, 2, 128, 0, 2, 0),     # negative q_frame0
+              AttnDesc(300, 2, 2**31 - 2, 1, 0, 2, 128, 0, 2, 0)):  # frame index overflows int
+        rc = lib().kvp_attn_bf16_noalloc(C.byref(io), C.byref(d),
+                                         hmap.ctypes.data_as(C.c_void_p), None, None)
+        assert rc == ERR_ARG, (d.tokens, d.frames, d.q_frame0, rc)
     io_dev_map = LayerIO(0x10000, 0x20000, 0x30000, 0x40000, 0, 0x50000, 600, 600, 0)
     rc = lib().kvp_attn_bf16_noalloc(C.byref(io_dev_map), C.byref(AttnDesc(300, 2, 0, 1, 0, 2, 128,
                                                                           0, 2, 0)),

@@ -77,6 +77,20 @@ def test_oracle_attention_matches_reference_golden():
         assert np.abs(got.reshape(F, Tq, D) - g[mode]).max() < 2e-6, mode
 
 
+def test_torch_restatement_matches_reference_golden():
+    """oracle/golden_torch.py, the CPU baseline bench.py times, gives the
+    reference golden's cross-frame outputs."""
+    import torch
+    from oracle import golden_torch
+    g = np.load(GOLDEN / "attn_golden.npz")
+    F, Tq, D = g["q"].shape
+    q, k, v = (torch.from_numpy(np.ascontiguousarray(g[n].reshape(-1, D))) for n in "qkv")
+    got = golden_torch.attention_frames(q, k, v, frames=F, tokens=Tq, heads=D // 128,
+                                        head_dim=128).numpy()
+    assert np.abs(got.reshape(F, Tq, D) - g["cross"]).max() < 2e-6
+    assert golden_torch.set_threads(2) == 2
+
+
 def test_reference_trace_and_golden_statistics():
     """Our restatement of the reference trace generator (kvp.traces) plus the
     attention oracle reproduce the reference's shipped 8-frame statistics."""
