@@ -455,9 +455,9 @@ def run_e2e(args, stack, scores, dev, stream, world, local_rank):
 
 
 def run_matrix(args) -> int:
-    """Per-frame cross-attention measurements (kvp/matrix.py), 1 GPU."""
+    """Per-frame cross-attention measurements (bench_matrix.py), 1 GPU."""
     import torch
-    from kvp import matrix
+    import bench_matrix as matrix
     torch.cuda.set_device(0)
     if args.matrix == 5:
         for row in matrix.run_config5(reps=max(1, args.reps), seed=args.seed,

@@ -1,14 +1,12 @@
-"""Per-frame cross-attention workloads: BASELINE config 5 (policy x budget x
-motion regime), config 2 (8-frame cross, Recency) and config 3 (50-frame
-trace, 30 layers, 5-frame causal window, ReuseWeighted).
+"""bench.py's per-frame measurements (`--matrix N`)
+(policy x budget x motion regime), config 2 (8-frame cross, Recency),
+config 3 (50-frame trace, 30 layers, 5-frame causal window,
+ReuseWeighted) and the extension legs (temporal reuse, QKV producer,
+motion producer, against torch SDPA, arena slot orders).
 
-One cell is the reference driver's per-frame loop
-(src/run_policy_experiment.cu:156-274) for F frames x T tokens, one layer of
-H heads, bf16: for every frame f one Session.step call selects, releases and
-stages the admitted tiles' rows into the arena, uploads the KVMap and sets
-the persisting window over the arena, and the tcgen05 kernel runs query
-frame f over key frames 0..f.  Everything is issued on one stream; unlike the reference there
-is no device synchronisation per frame.
+Measurement code, not part of the library: one cell is the reference
+driver's per-frame loop (src/run_policy_experiment.cu:156-274) as the
+library runs it (kvp.frames.run_frames), timed with CUDA events.
 
 `cell_order` fixes the order of the cells (regime, budget, policy) and the
 repetition order: forward, then backward (ABBA), as the reference's variance
@@ -24,9 +22,10 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .attention import attn_bf16, read_status
-from .session import Session
-from .traces import motion_config2, motion_config3, motion_config5, qkv
+from kvp.attention import attn_bf16, read_status
+from kvp.frames import run_frames, run_reuse_frames
+from kvp.session import Session
+from kvp.traces import motion_config2, motion_config3, motion_config5, qkv
 
 POLICY_ORDER = ("none", "uniform", "recency", "motion", "reuse_weighted")
 BUDGET_FRACS = (0.10, 0.25, 0.50, 1.00)
@@ -49,90 +48,11 @@ def cross_flops(frames: int, tokens: int, heads: int, head_dim: int = 128) -> fl
     return float(sum(4 * tokens * (f + 1) * tokens * head_dim for f in range(frames)) * heads)
 
 
-def run_frames(q, k, v, out, scores, *, policy: str, set_aside: int, frames: int, tokens: int,
-               heads: int, stream: int, streaming: bool = False, events=None,
-               mode: str = "cross") -> dict:
-    """One pass over all frames of a cell.  The Session (device buffers) is
-    created before and destroyed after the optional (start, end) CUDA events,
-    so a timed pass holds only the per-frame work.  mode "cross" (keys of
-    frames 0..f) or "intra" (keys of frame f)."""
-    hidden = heads * 128
-    amode = "causal" if mode == "cross" else "intra"
-    s = Session(mode=mode, policy=policy, frames=frames, tokens=tokens, hidden=hidden,
-                elem_bytes=2, set_aside=set_aside, streaming=streaming, layers=1)
-    copies = staged = 0
-    try:
-        if events:
-            events[0].record()
-        kp, vp = [k.data_ptr()], [v.data_ptr()]
-        for f in range(frames):
-            s.step(f, scores, kp, vp, window_layer=0, stream=stream)
-            st = s.info()
-            copies += st.copies
-            staged += st.staged_bytes
-            if policy != "none":
-                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
-                          mode=amode, kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(0),
-                          arena_rows=s.cap_rows, stream=stream)
-            else:
-                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
-                          mode=amode, stream=stream)
-        if policy != "none":
-            s.clear_window(stream)
-        if events:
-            events[1].record()
-        torch.cuda.synchronize()   # the Session's buffers outlive every launch
-        s.finish()
-    finally:
-        s.close()
-    return {"copies": copies, "staged_bytes": staged}
-
-
-def run_reuse_frames(q, k, v, out, scores, reuse, *, policy: str, set_aside: int, frames: int,
-                     tokens: int, heads: int, stream: int, events=None) -> dict:
-    """Temporal-reuse pass: per frame f the Session (mode "reuse") selects
-    among frame f's tiles, keeps the slots of tiles it keeps selecting, and
-    stages only new or changed tiles' rows; the kernel runs frame f's
-    queries over frame f's keys through the KVMap (intra).  A kept,
-    unchanged tile is read from the slot written in an earlier frame."""
-    hidden = heads * 128
-    s = Session(mode="reuse", policy=policy, frames=frames, tokens=tokens, hidden=hidden,
-                elem_bytes=2, set_aside=set_aside, streaming=True, layers=1)
-    tot = {"copies": 0, "restaged": 0, "hits": 0, "staged_bytes": 0}
-    try:
-        if events:
-            events[0].record()
-        kp, vp = [k.data_ptr()], [v.data_ptr()]
-        for f in range(frames):
-            s.step(f, scores, kp, vp, reuse=reuse, window_layer=0, stream=stream)
-            st = s.info()
-            tot["copies"] += st.copies
-            tot["restaged"] += st.restaged
-            tot["hits"] += st.hits
-            tot["staged_bytes"] = st.staged_bytes
-            if policy != "none":
-                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
-                          mode="intra", kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(0),
-                          arena_rows=s.cap_rows, stream=stream)
-            else:
-                attn_bf16(q, k, v, out, tokens=tokens, frames=1, q_frame0=f, heads=heads,
-                          mode="intra", stream=stream)
-        if policy != "none":
-            s.clear_window(stream)
-        if events:
-            events[1].record()
-        torch.cuda.synchronize()
-        s.finish()
-    finally:
-        s.close()
-    return tot
-
-
 def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: int = 12,
                 seed: int = 0, max_persist: int | None = None, streaming: bool = False,
                 device="cuda") -> list[dict]:
     """All 40 cells, `reps` repetitions each in ABBA order; one dict per cell."""
-    from ._lib import DeviceInfo, lib
+    from kvp._lib import DeviceInfo, lib
     import ctypes as C
     if max_persist is None:
         info = DeviceInfo()
@@ -226,7 +146,7 @@ def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: i
     into every layer's arena with one launch, then per layer the persisting
     window over its arena and one attention launch (query frame f, key frames
     max(0, f-window+1)..f).  Also the None policy on the same inputs."""
-    from ._lib import DeviceInfo, lib
+    from kvp._lib import DeviceInfo, lib
     import ctypes as C
     info = DeviceInfo()
     lib().kvp_query_device(-1, C.byref(info))
@@ -312,8 +232,8 @@ def run_reuse_matrix(*, reps: int = 3, frames: int = 16, tokens: int = 1560, hea
     Traces: AR(1) rho 0.9 (BASELINE config 2's motion model, temporally
     coherent) and config 5 'high' (i.i.d. per frame); reuse flags by the
     percentile-50 rule."""
-    from ._lib import DeviceInfo, lib
-    from .traces import hold_reused_tiles, reuse_flags
+    from kvp._lib import DeviceInfo, lib
+    from kvp.traces import hold_reused_tiles, reuse_flags
     import ctypes as C
     if max_persist is None:
         info = DeviceInfo()
@@ -401,9 +321,9 @@ def run_producer(*, reps: int = 20, warmup: int = 3, frames: int = 21, tokens: i
     x (100 MB) and the outputs (300 MB) exceed L2; W (14 MB) stays in it.
     Arena equality of the fused and gather paths is checked by the GPU tests
     (tests/test_gpu_producer.py)."""
-    from ._lib import DeviceInfo, lib
-    from .producer import layernorm, qkv_project
-    from .traces import motion_config4
+    from kvp._lib import DeviceInfo, lib
+    from kvp.producer import layernorm, qkv_project
+    from kvp.traces import motion_config4
     import ctypes as C
     if set_aside is None:
         info = DeviceInfo()
@@ -490,8 +410,8 @@ def run_motion(*, frames: int = 20, reps: int = 5, seed: int = 0, cpu_pairs: int
     reference's own flow call (OpenCV Farneback on the host cores, the
     threads OpenCV uses) timed on `cpu_pairs` pairs of the same clip."""
     import time
-    from .motion import MotionProducer
-    from .traces import synthetic_video
+    from kvp.motion import MotionProducer
+    from kvp.traces import synthetic_video
     clip = synthetic_video(frames, seed=seed)
     mp = MotionProducer()
     d = torch.from_numpy(clip).to(device)

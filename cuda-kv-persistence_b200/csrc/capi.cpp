@@ -38,6 +38,31 @@ int* status_word() {
     return words[dev];
 }
 
+bool primary_context_active(int device) {
+    typedef int (*DeviceGetFn)(int*, int);
+    typedef int (*CtxStateFn)(int, unsigned*, int*);
+    static DeviceGetFn device_get = nullptr;
+    static CtxStateFn ctx_state = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuDeviceGet", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            device_get = reinterpret_cast<DeviceGetFn>(p);
+        if (cudaGetDriverEntryPoint("cuDevicePrimaryCtxGetState", &p, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            ctx_state = reinterpret_cast<CtxStateFn>(p);
+    });
+    if (!device_get || !ctx_state) return true;
+    int dev = 0;
+    if (device_get(&dev, device) != 0) return true;
+    unsigned flags = 0;
+    int active = 1;
+    if (ctx_state(dev, &flags, &active) != 0) return true;
+    return active != 0;
+}
+
 void set_error(const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);

@@ -30,6 +30,18 @@ KVTileManager::KVTileManager(size_t budget_bytes, size_t max_window_bytes, unsig
 }
 
 KVTileManager::~KVTileManager() {
+    // A caller may reset the device before destroying its manager (the
+    // reference's driver calls cudaDeviceReset() at the end of main(), while
+    // its manager is still in scope, src/run_policy_experiment.cu:315).  The
+    // handles made in the destroyed context must not reach CUDA again: the
+    // reset released them, and an event of a destroyed context faults the
+    // driver.  The manager then only forgets them.
+    if (!dry_run() && device_ >= 0 && !primary_context_active(device_)) {
+        std::lock_guard<std::mutex> g(g_registry_mu);
+        g_registry.erase(std::remove(g_registry.begin(), g_registry.end(), this), g_registry.end());
+        if (initialized_ && --g_live_initialised == 0) g_limit_saved = false;
+        return;
+    }
     clear();
     flush();
     if (!dry_run()) {
@@ -136,6 +148,7 @@ void KVTileManager::clear() {
 bool KVTileManager::arena_init(size_t capacity_bytes, size_t row_stride_floats) {
     // :88-97
     if (arena_ready_) return false;
+    if (!dry_run() && device_ < 0) cudaGetDevice(&device_);
     if (!dry_run() && cudaMalloc(&arena_, capacity_bytes) != cudaSuccess) {
         arena_ = nullptr;
         set_error("arena cudaMalloc(%zu) failed", capacity_bytes);
@@ -310,6 +323,7 @@ void KVTileManager::queue_copy(void* dst, const void* src, size_t bytes) {
 
 int KVTileManager::flush() {
     if (pending_.empty() || dry_run()) return KVP_OK;
+    if (device_ < 0) KVP_CUDA(cudaGetDevice(&device_));
     const size_t n = pending_.size();
     if (n > ops_cap_) {
         if (ops_done_) cudaEventSynchronize(ops_done_);

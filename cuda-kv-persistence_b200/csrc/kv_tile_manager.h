@@ -156,6 +156,7 @@ private:
     size_t saved_limit_ = 0;
     std::vector<WindowRecord> window_log_;
     long reset_calls_ = 0;
+    int device_ = -1;             // device of the arena and copy-list buffers, -1 before any
 };
 
 // Issues the queued copies of every live manager (stream-ordered on each

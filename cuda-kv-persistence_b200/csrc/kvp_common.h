@@ -30,6 +30,12 @@ constexpr int KVP_STATUS_ALIGN = 4;    // dynamic shared memory not 1024-byte al
 // kvp_read_status reads and clears it).  nullptr if it cannot be allocated.
 int* status_word();
 
+// False when the primary context of `device` is not active, e.g. after a
+// cudaDeviceReset() by this or another CUDA runtime in the process: handles
+// made in the context before it was destroyed must not be passed to CUDA.
+// True when the state cannot be queried.
+bool primary_context_active(int device);
+
 // Records the message of the last failure on this thread.
 void set_error(const char* fmt, ...);
 const char* last_error();

@@ -1,4 +1,4 @@
-"""The per-frame cross-attention harness (kvp/matrix.py) on a device: the
+"""The per-frame cross-attention loop (kvp/frames.py) on a device: the
 reference driver's loop for arena and streaming sessions produces outputs
 bitwise identical to the None policy, within tolerance of the oracle."""
 
@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("streaming", [False, True])
 def test_per_frame_loop_policies_bitwise(cuda, streaming):
-    from kvp import matrix
+    from kvp import frames as matrix
     from kvp.attention import read_status
     from kvp.traces import motion_config5, qkv
     F, T, H = 4, 300, 2

@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 
 def test_motion_to_reuse_to_attention(cuda):
-    from kvp import matrix
+    from kvp import frames as matrix
     from kvp.attention import read_status
     from kvp.motion import MotionProducer, threshold
     from kvp.traces import hold_reused_tiles, qkv, synthetic_video

@@ -35,7 +35,7 @@ def _inputs(seed):
 
 
 def _run(q, k, v, scores, reuse, policy, set_aside):
-    from kvp import matrix
+    from kvp import frames as matrix
     out = torch.zeros_like(q)
     stream = int(torch.cuda.current_stream().cuda_stream)
     tot = matrix.run_reuse_frames(q, k, v, out, scores, reuse, policy=policy, set_aside=set_aside,

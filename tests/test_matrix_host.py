@@ -1,4 +1,4 @@
-"""Host-side checks of the per-frame cross-attention harness (kvp/matrix.py)."""
+"""Host-side checks of the per-frame cross-attention harness (bench_matrix.py)."""
 
 from __future__ import annotations
 
@@ -6,7 +6,7 @@ import pytest
 
 
 def test_config5_cells_and_flops():
-    from kvp import matrix
+    import bench_matrix as matrix
     cells = matrix.cell_order()
     assert len(cells) == 5 * 4 * 2
     assert {c.policy for c in cells} == {"none", "uniform", "recency", "motion", "reuse_weighted"}
@@ -29,7 +29,7 @@ def test_config5_regimes_shapes():
 
 
 def test_config3_flops():
-    from kvp import matrix
+    import bench_matrix as matrix
     # 50 frames, window of 5 frames: 240 frame-units per (layer, head); 1.0765e14 FLOP
     assert matrix.window_flops(50, 1560, 12, 30, 5) == pytest.approx(1.0765e14, rel=1e-4)
     assert matrix.window_flops(3, 1560, 12, 1, 5) == pytest.approx(matrix.cross_flops(3, 1560, 12))
@@ -40,7 +40,7 @@ def test_slot_order_maps(order):
     """--matrix 10 maps: whole 16-row tiles, every slot used once; ascending
     and descending runs inside each tile as named."""
     import torch
-    from kvp.matrix import slot_order_map
+    from bench_matrix import slot_order_map
     m, rows, slots = slot_order_map(32760, 16, 640, order, seed=1, device="cpu")
     assert rows.numel() == 10240 and int((m >= 0).sum()) == 10240
     assert sorted(slots.tolist()) == list(range(10240))
