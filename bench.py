@@ -48,7 +48,12 @@ sys.path.insert(0, str(PKG))
 FRAMES, TOKENS, LAYERS, HEADS, HEAD_DIM = 21, 1560, 30, 12, 128
 N_PAIRS = LAYERS * HEADS
 METRIC = "remapped-MHA TFLOP/s"
-KERNEL = "attn_bf16_sm100_kernel"
+
+
+def attention_kernel() -> str:
+    """The bf16 kernel kvp_attn_bf16 launches: the one-SM kernel unless
+    KVP_ATTN_PAIR=1 selects the SM-pair kernel."""
+    return "attn_pair_sm100_kernel" if os.environ.get("KVP_ATTN_PAIR") == "1" else "attn_bf16_sm100_kernel"
 
 
 def stack_flops(frames=FRAMES, tokens=TOKENS, pairs=N_PAIRS):
@@ -63,13 +68,36 @@ def measured_peaks():
     return 1400.0, 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """dram read+write bytes per attention launch from the committed ncu summary."""
-    for p in sorted((ROOT / "profiles").glob("*.md")):
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
-        if m and "stack21" in p.name:
+def profiled_traffic(kernel: str):
+    """dram read+write bytes per attention launch of `kernel` from the
+    committed ncu summary of one stack layer (profiles/*stack21*.md)."""
+    for p in sorted((ROOT / "profiles").glob("*stack21*.md")):
+        text = p.read_text()
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", text)
+        if m and kernel in text:
             return float(m.group(1))
     return None
+
+
+def profiled_dram_per_step():
+    """DRAM bytes read per config-4 step under the bench's policy and under
+    None, from the committed ncu summary profiles/ncu_dram_stack21_step.md
+    (one layer captured, scaled to the 30-layer step there)."""
+    p = ROOT / "profiles" / "ncu_dram_stack21_step.md"
+    if not p.exists():
+        return None
+    text = p.read_text()
+    vals = {}
+    for key in ("read_bytes_per_step", "none_read_bytes_per_step", "write_bytes_per_step",
+                "none_write_bytes_per_step"):
+        m = re.search(key + r":\s*([0-9.eE+]+)", text)
+        if m:
+            vals[key] = float(m.group(1))
+    if "read_bytes_per_step" not in vals or "none_read_bytes_per_step" not in vals:
+        return None
+    vals["ratio"] = round(vals["read_bytes_per_step"] / vals["none_read_bytes_per_step"], 4)
+    vals["source"] = "profiles/ncu_dram_stack21_step.md (ncu dram__bytes_read.sum, one layer x 30)"
+    return vals
 
 
 class ClockSampler:
@@ -223,7 +251,9 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
             c.o = buf[off:off + n].view(c.o.shape)
             off += n
 
-    launches_per_step = len(stack.chunks) + (len(stack.sessions) if stack.persist else 0)
+    attn_launches = (-(-len(stack.chunks) // args.group) if args.launch == "multi"
+                     else len(stack.chunks))
+    launches_per_step = attn_launches + (len(stack.sessions) if stack.persist else 0)
     attn_events = []
     gather_done = [None, None]   # last all-gather that read each output buffer
 
@@ -234,15 +264,25 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
         bind_outputs(flat[b])
         with torch.cuda.stream(stream):
             stack.plan_and_stage(scores, sp)
-            for c in stack.chunks:
+            if args.launch == "multi":
                 if timed:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e1 = torch.cuda.Event(enable_timing=True)
                     e0.record(stream)
-                stack.attend(c, sp)
+                stack.attend_all(sp, group=args.group)
                 if timed:
                     e1.record(stream)
                     attn_events.append((e0, e1))
+            else:
+                for c in stack.chunks:
+                    if timed:
+                        e0 = torch.cuda.Event(enable_timing=True)
+                        e1 = torch.cuda.Event(enable_timing=True)
+                        e0.record(stream)
+                    stack.attend(c, sp)
+                    if timed:
+                        e1.record(stream)
+                        attn_events.append((e0, e1))
             if stack.persist and stack.use_window:
                 stack.sessions[0].clear_window(sp)
         if world > 1:
@@ -318,7 +358,7 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
         roofline = {"bound": "tensor", "achieved": round(achieved, 2) if achieved else None,
                     "peak": peak, "unit": "TFLOP/s",
                     "frac": round(achieved / peak, 4) if achieved else None,
-                    "traffic": profiled_traffic(), "kernel": KERNEL,
+                    "traffic": profiled_traffic(attention_kernel()), "kernel": attention_kernel(),
                     "peak_kind": f"{peak_kind} bf16 sustained (cuBLAS)",
                     "flop_per_launch": per_launch_flops,
                     "avg_launch_ms": round(attn_ms / max(n_attn, 1), 4)}
@@ -339,11 +379,13 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
                        "tokens_per_frame": TOKENS, "layers": LAYERS, "heads": HEADS,
                        "head_dim": HEAD_DIM, "pairs": args.pairs, "policy": args.policy,
                        "set_aside_bytes": set_aside, "persisting_window": args.window,
+                       "attention_launches": f"{args.launch} ({attn_launches} per step)",
                        "mask": "block-causal by frame",
                        "flop_per_step": total_flops,
                        "l2": "inputs 12.1 GB exceed the 126 MB L2 (no flush needed)",
                        "parallelism": f"pairs/{world}" + (" + nccl all_gather" if world > 1 else "")},
             "roofline": roofline,
+            "dram": profiled_dram_per_step(),
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
@@ -482,7 +524,7 @@ def run_matrix(args) -> int:
             print(json.dumps({"metric": "temporal reuse cell", **row}), flush=True)
     elif args.matrix == 3:
         for row in matrix.run_config3(reps=max(1, args.reps), seed=args.seed,
-                                      streaming=args.streaming):
+                                      streaming=args.streaming, launch=args.launch):
             print(json.dumps({"metric": "config3", **row}), flush=True)
     else:
         print(json.dumps({"metric": "config2", **matrix.run_config2(reps=max(1, args.reps),
@@ -504,6 +546,10 @@ def main() -> int:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--pairs", type=int, default=N_PAIRS,
                     help="(layer, head) pairs of the stack (360 = the full config; fewer only for profiling)")
+    ap.add_argument("--launch", choices=["multi", "layer"], default="multi",
+                    help="attention launches: several layer chunks per launch (kvp_attn_bf16_multi) "
+                         "or one per layer chunk (kvp_attn_bf16)")
+    ap.add_argument("--group", type=int, default=12, help="layer chunks per launch with --launch multi")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

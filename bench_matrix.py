@@ -22,7 +22,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from kvp.attention import attn_bf16, read_status
+from kvp.attention import attn_bf16, attn_bf16_multi, read_status
 from kvp.frames import run_frames, run_reuse_frames
 from kvp.session import Session
 from kvp.traces import motion_config2, motion_config3, motion_config5, qkv
@@ -140,12 +140,15 @@ def window_flops(frames: int, tokens: int, heads: int, layers: int, window: int,
 
 def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: int = 12,
                 layers: int = 30, window: int = 5, seed: int = 0, streaming: bool = False,
-                device="cuda") -> list[dict]:
+                device="cuda", launch: str = "multi") -> list[dict]:
     """Config 3: per frame one admission (ReuseWeighted over the window's
     tiles, budget = the device's max persisting L2), the admitted rows staged
-    into every layer's arena with one launch, then per layer the persisting
-    window over its arena and one attention launch (query frame f, key frames
-    max(0, f-window+1)..f).  Also the None policy on the same inputs."""
+    into every layer's arena with one launch, then the attention of query
+    frame f over key frames max(0, f-window+1)..f in every layer: launch
+    "layer" sets each layer's persisting window over its arena and launches
+    that layer alone (the reference driver's structure); launch "multi" runs
+    the layers 12 to a launch (kvp_attn_bf16_multi) under one window over the
+    first layer's arena.  Also the None policy on the same inputs."""
     from kvp._lib import DeviceInfo, lib
     import ctypes as C
     info = DeviceInfo()
@@ -176,6 +179,20 @@ def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: i
                 if persist:
                     s.upload(stream)
                     s.stage([t.data_ptr() for t in ks], [t.data_ptr() for t in vs], stream)
+                if launch == "multi":
+                    group = []
+                    for layer in range(layers):
+                        L = dict(q=qs[layer], k=ks[layer], v=vs[layer], out=outs[layer], heads=heads)
+                        if persist:
+                            L.update(kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(layer),
+                                     arena_rows=s.cap_rows)
+                        group.append(L)
+                    for g0 in range(0, layers, 12):
+                        if persist:
+                            s.window(g0, stream)
+                        attn_bf16_multi(group[g0:g0 + 12], tokens=tokens, frames=1, q_frame0=f,
+                                        mode="causal", window=window, stream=stream)
+                    continue
                 for layer in range(layers):
                     if persist:
                         s.window(layer, stream)
@@ -213,7 +230,8 @@ def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: i
             one_pass(policy, (e0, e1))
             ts.append(e0.elapsed_time(e1))
         t = float(np.mean(ts))
-        res.append({"config": 3, "policy": policy, "streaming": streaming, "frames": frames,
+        res.append({"config": 3, "policy": policy, "streaming": streaming, "launch": launch,
+                    "frames": frames,
                     "layers": layers,
                     "window": window, "set_aside_bytes": budget, "ms_mean": round(t, 3),
                     "ms_runs": [round(x, 3) for x in ts],

@@ -43,7 +43,8 @@ def _deps_newer(obj: Path, src: Path) -> bool:
     t = obj.stat().st_mtime
     if src.stat().st_mtime > t:
         return True
-    headers = list(CSRC.glob("*.h")) + list((HERE.parent / "include").rglob("*.h"))
+    headers = (list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) +
+               list((HERE.parent / "include").rglob("*.h")))
     return any(h.stat().st_mtime > t for h in headers)
 
 

@@ -51,8 +51,10 @@
 #include <mutex>
 #include <unordered_map>
 
+#include "attn_pair_sm100.h"
 #include "attn_sm100.h"
 #include "kvp_common.h"
+#include "attn_softmax_sm100.cuh"
 #include "sm100_ptx.h"
 
 namespace kvp {
@@ -60,6 +62,7 @@ namespace kvp {
 namespace {
 
 using namespace ptx;
+using namespace attn_dev;
 
 constexpr int kBM = 128;           // query rows per query tile
 constexpr int kQTiles = 2;         // query tiles per CTA
@@ -75,14 +78,6 @@ constexpr int kRegsLow = 104;      // registers per thread, warps 0-3 (producers
 constexpr int kRegsHigh = 200;     // registers per thread, warps 4-11 (softmax)
 static_assert(kRegsLow * 128 + 2 * kRegsHigh * 128 <= 65536, "register split exceeds the SM");
 constexpr float kRedoSum = 256.f;  // a tile row sum above this recomputes with the new max
-// Which of the 16 column pairs of each 32-column chunk take the FMA-pipe
-// exponential (ex2_poly2) instead of MUFU: bit p = pair p.  Two pairs in
-// sixteen (one exponential in eight) measured fastest on the 21-frame
-// layer; four, six and eight pairs were 1 %, 9 % and 12 % slower.
-#ifndef KVP_POLY_PAIRS
-#define KVP_POLY_PAIRS 0x8080u
-#endif
-constexpr uint32_t kPolyPairs = KVP_POLY_PAIRS;
 
 struct __align__(1024) Smem {
     uint8_t q[kQTiles][kTileBytes];
@@ -110,17 +105,53 @@ struct TmaMaps {
     CUtensorMap a1;                 // arena, box 64 x 1 (TMA gather of scattered slots)
 };
 
-struct Params {
+// One layer's tensors (a launch covers one or several of them: a segment
+// table).  Segment i owns CTAs [cta0, cta0 + nheads * items_per_head).
+struct Seg {
+    TmaMaps maps;
     const __nv_bfloat16* k;      // base rows, for mixed groups
     const __nv_bfloat16* v;
     const __nv_bfloat16* arena;
     const long long* kvmap;
     __nv_bfloat16* out;
-    int* status;
     long long q_rows, kv_rows, arena_rows;
-    int D, T, frames, q_frame0, mode, window, head0, nheads, flat, items_per_head, n_qt, n_pairs;
+    int D, head0, nheads, cta0;
     int base_boxes, arena_boxes;   // box kinds usable (heights <= tensor rows); 0 = no arena TMA
     int arena_gather;              // 1 = maps.a1 is encoded (scattered arena groups by TMA gather)
+};
+
+// A segment's scalars, copied into registers at the start of the kernel: a
+// launch over several segments indexes its table with the CTA's segment, and
+// reads through that runtime address would otherwise repeat in the loops.
+struct SegHot {
+    const __nv_bfloat16* k;
+    const __nv_bfloat16* v;
+    const __nv_bfloat16* arena;
+    const long long* kvmap;
+    __nv_bfloat16* out;
+    long long q_rows, kv_rows, arena_rows;
+    int D, head0, nheads, cta0, base_boxes, arena_boxes, arena_gather;
+};
+
+__device__ __forceinline__ SegHot seg_hot(const Seg& g) {
+    return SegHot{g.k, g.v, g.arena, g.kvmap, g.out, g.q_rows, g.kv_rows, g.arena_rows,
+                  g.D, g.head0, g.nheads, g.cta0, g.base_boxes, g.arena_boxes, g.arena_gather};
+}
+
+// Segments per launch: 1 for kvp_attn_bf16, up to kMaxSegs for
+// kvp_attn_bf16_multi (the table is a kernel parameter, 2.3 KB a segment).
+constexpr int kMaxSegs = 12;
+
+template <int kSegs>
+struct SegTable {
+    Seg seg[kSegs];
+};
+
+// What every segment of a launch shares: the frames and masking, the
+// split workspace, the status word.
+struct Params {
+    int* status;
+    int T, frames, q_frame0, mode, window, flat, items_per_head, n_qt, n_pairs, n_segs;
     float scale_log2;
     // Key-range split (per-frame tiling only): splits > 1 writes fp32 partial
     // (O, m, l) to ws instead of bf16 output; combine_splits_kernel merges.
@@ -204,62 +235,6 @@ constexpr uint32_t idesc_bf16(bool b_mn_major) {
            ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot per pair).
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-// 2^x for a pair on the FMA/ALU pipes (f32x2 arithmetic): x = n + f with
-// n = round(x) and f in [-1/2, 1/2], 2^f by a cubic fitted here by iteratively reweighted least squares on the
-// relative error (max relative error 1.4e-4 over x in [-126, 8], against bf16's
-// 3.9e-3 rounding of P), 2^n added to the exponent bits.  Inputs below -126
-// are clamped to -126 (the result stays a positive number below 2^-125,
-// negligible in the row sum and against any unmasked P; -inf lands there
-// too), inputs above 127 to 127 (a finite 2^127-ish value, so an overgrown
-// speculative exponent still shows up in the row sum instead of wrapping
-// the exponent bits).
-__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
-    const uint64_t x = f2_pack(fminf(fmaxf(x0, -126.f), 127.f), fminf(fmaxf(x1, -126.f), 127.f));
-    const uint64_t magic = f2_pack(12582912.f, 12582912.f);
-    const uint64_t t = f2_add(x, magic);
-    const uint64_t f = f2_sub(x, f2_sub(t, magic));
-    uint64_t q = f2_fma(f2_pack(5.517162719e-02f, 5.517162719e-02f), f, f2_pack(2.426111432e-01f, 2.426111432e-01f));
-    q = f2_fma(q, f, f2_pack(6.932609953e-01f, 6.932609953e-01f));
-    q = f2_fma(q, f, f2_pack(9.999280725e-01f, 9.999280725e-01f));
-    float t0, t1, q0, q1;
-    f2_unpack(t, t0, t1);
-    f2_unpack(q, q0, q1);
-    // t = 1.5*2^23 + n has bits 0x4B400000 + n, and 0x4B400000 << 23 wraps to
-    // zero, so (bits(t) << 23) == n << 23.
-    y0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-    y1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
-}
-
 // --------------------------------------------------------------- work item
 struct QTile {
     long long row0;      // first query row (absolute in Q/out)
@@ -279,11 +254,12 @@ struct Work {
     QTile t[kQTiles];
 };
 
-__device__ __forceinline__ Work decode_work(const Params& P) {
+__device__ __forceinline__ Work decode_work(const Params& P, const SegHot& S) {
     Work w;
-    const int h_local = blockIdx.x / P.items_per_head;
-    const int i = blockIdx.x % P.items_per_head;
-    w.head = P.head0 + h_local;
+    const int blk = (int)blockIdx.x - S.cta0;
+    const int h_local = blk / P.items_per_head;
+    const int i = blk % P.items_per_head;
+    w.head = S.head0 + h_local;
     w.chunk = 0;
     const long long T = P.T;
     if (P.flat) {
@@ -363,78 +339,6 @@ __device__ __forceinline__ Work decode_work(const Params& P) {
     return w;
 }
 
-// ----------------------------------------------------------- softmax pieces
-// One S row (this thread's TMEM lane, 128 columns) -> P = 2^(s*sl2 - m) as
-// packed bf16 pairs in pk, returns the fp32 row sum of P.  Columns at or
-// past `left` are masked (-inf) when kMask.  One exponential in eight runs
-// on the FMA pipe (ex2_poly2), the rest on MUFU; scaling and the row sum use
-// f32x2 arithmetic.
-template <bool kMask>
-__device__ __forceinline__ float exp_row(uint32_t s_addr, float m, float sl2, int left, uint32_t (&pk)[64]) {
-    const uint64_t sl2x2 = f2_pack(sl2, sl2);
-    const uint64_t negm2 = f2_pack(-m, -m);
-    uint64_t acc[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i] = 0ull;   // (+0, +0)
-    // 32-column chunks, software-pipelined: chunk h+1 is loading from TMEM
-    // while chunk h is computed.
-    uint32_t sa[32], sb[32];
-    KVP_TMEM_LD32(s_addr, sa);
-    KVP_TMEM_WAIT_LD_DEP(sa);
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-        uint32_t(&cur)[32] = (h & 1) ? sb : sa;
-        uint32_t(&nxt)[32] = (h & 1) ? sa : sb;
-        if (h < 3) KVP_TMEM_LD32(s_addr + 32 * (h + 1), nxt);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-            float s0 = __uint_as_float(cur[c]);
-            float s1 = __uint_as_float(cur[c + 1]);
-            if (kMask) {
-                if (32 * h + c >= left) s0 = -INFINITY;
-                if (32 * h + c + 1 >= left) s1 = -INFINITY;
-            }
-            float x0, x1, p0, p1;
-            f2_unpack(f2_fma(f2_pack(s0, s1), sl2x2, negm2), x0, x1);
-            if ((kPolyPairs >> (c >> 1)) & 1u) {   // selected pairs on the FMA pipe
-                ex2_poly2(x0, x1, p0, p1);
-            } else {
-                p0 = ex2_approx(x0);
-                p1 = ex2_approx(x1);
-            }
-            acc[(c >> 1) & 3] = f2_add(acc[(c >> 1) & 3], f2_pack(p0, p1));
-            pk[16 * h + (c >> 1)] = pack_bf16(p0, p1);
-        }
-        if (h < 3) KVP_TMEM_WAIT_LD_DEP(nxt);
-    }
-    const uint64_t a2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
-    float lo, hi;
-    f2_unpack(a2, lo, hi);
-    return lo + hi;
-}
-
-// Row max of one S row (raw scores), masked as in exp_row.
-template <bool kMask>
-__device__ __forceinline__ float max_row(uint32_t s_addr, int left) {
-    float mx[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-        uint32_t sr[32];
-        KVP_TMEM_LD32(s_addr + 32 * h, sr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-            float s = __uint_as_float(sr[c]);
-            if (kMask && 32 * h + c >= left) s = -INFINITY;
-            mx[c & 7] = fmaxf(mx[c & 7], s);
-        }
-    }
-    return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-}
-
 // Stage release by the softmax: valid when the tile issuing
 // the last S GEMM of every K/V step also issues the PV GEMMs of the step
 // before it -- Q1 when it has the full key span (n1 == max), or Q0 alone.
@@ -444,8 +348,9 @@ __device__ __forceinline__ float max_row(uint32_t s_addr, int left) {
 __device__ __forceinline__ bool soft_release(int n0, int n1) { return !(n1 > 0 && n1 < n0); }
 
 // ------------------------------------------------------------------ kernel
+template <int kSegs>
 __global__ void __launch_bounds__(kThreads, 1)
-attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_constant__ Params P) {
+attn_bf16_sm100_kernel(const __grid_constant__ SegTable<kSegs> tab, const __grid_constant__ Params P) {
     extern __shared__ uint8_t smem_raw[];
     // The layout needs a 1024-byte aligned base (128B-swizzle atoms) and uses
     // nearly all of the 227 KB, so there is no room to realign: refuse instead.
@@ -456,7 +361,13 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const Work w = decode_work(P);
+    int si = 0;
+#pragma unroll
+    for (int i = 1; i < kSegs; ++i)
+        if (i < P.n_segs && (int)blockIdx.x >= tab.seg[i].cta0) si = i;
+    const TmaMaps& maps = tab.seg[si].maps;
+    const SegHot S = seg_hot(tab.seg[si]);
+    const Work w = decode_work(P, S);
     const int n_tiles = w.n_tiles;
 
     if (threadIdx.x == 0) {
@@ -488,7 +399,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
-    const int D = P.D;
+    const int D = S.D;
     const int hcol = w.head * kDH;
     // Register split: the producer / MMA warpgroup hands registers to the two
     // softmax warpgroups.  The host checks before launch that the kernel's
@@ -514,10 +425,10 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                 const long long qr0 = w.t[q].row0;
                 uint32_t qbytes = 0;
                 for (int g = 0; g < kBM / 8; ++g)
-                    if (qr0 + 8 * g < P.q_rows) qbytes += 2 * kGroupPanel;
+                    if (qr0 + 8 * g < S.q_rows) qbytes += 2 * kGroupPanel;
                 mbar_arrive_expect_tx(&sm.bar_q[q], qbytes);
                 for (int g = 0; g < kBM / 8; ++g) {
-                    if (qr0 + 8 * g >= P.q_rows) break;
+                    if (qr0 + 8 * g >= S.q_rows) break;
                     for (int p = 0; p < 2; ++p)
                         tma_load_2d(sm.q[q] + p * kPanel + g * kGroupPanel, &maps.q8, hcol + 64 * p,
                                     (int)(qr0 + 8 * g), &sm.bar_q[q]);
@@ -529,7 +440,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         uint64_t* bar_empty = op == 0 ? sm.bar_kempty : sm.bar_vempty;
         uint8_t* ring = op == 0 ? sm.k[0] : sm.v[0];
         const CUtensorMap* base_maps = maps.kv[op];
-        const __nv_bfloat16* base = op == 0 ? P.k : P.v;
+        const __nv_bfloat16* base = op == 0 ? S.k : S.v;
         const int acol = (op == 0 ? 0 : D) + hcol;     // column of this operand in an arena row
         int last_armed = -1;
         // KVMap rows of a tile are read one tile ahead, so their L2 latency
@@ -539,7 +450,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const long long row = rr0 + 4 * lane + i;
-                mm[i] = (jj < n_tiles && row < w.khi && P.kvmap) ? __ldg(P.kvmap + row) : -1;
+                mm[i] = (jj < n_tiles && row < w.khi && S.kvmap) ? __ldg(S.kvmap + row) : -1;
             }
         };
         long long m_next[4];
@@ -556,7 +467,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 pad[i] = r0 + 4 * lane + i >= w.khi;
-                if (m[i] >= P.arena_rows || (m[i] >= 0 && !P.arena)) {
+                if (m[i] >= S.arena_rows || (m[i] >= 0 && !S.arena)) {
                     if (op == 0) atomicOr(P.status, KVP_STATUS_MAP);
                     m[i] = -1;   // out-of-range entry: read the base row
                 }
@@ -573,20 +484,20 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
             const bool p_pad0 = __shfl_xor_sync(0xffffffffu, pad[0], 1);
             const bool group_pad = even ? pad[0] : p_pad0;
             const bool g_base = all_neg && p_neg && !group_pad;
-            const bool g_arena = P.arena_boxes > 0 && asc && p_asc && (even ? p_m0 == m[0] + 4 : m[0] == p_m0 + 4);
+            const bool g_arena = S.arena_boxes > 0 && asc && p_asc && (even ? p_m0 == m[0] + 4 : m[0] == p_m0 + 4);
             // Every row of the group in the arena, in any slot order (LIFO slot
             // reuse leaves descending runs), none of it padding: two TMA
             // gathers of four rows per panel.
             const bool all_arena = !pad[3] && m[0] >= 0 && m[1] >= 0 && m[2] >= 0 && m[3] >= 0;
             const bool p_all_arena = __shfl_xor_sync(0xffffffffu, all_arena, 1);
-            const bool g_gather = P.arena_gather && all_arena && p_all_arena && !g_arena;
+            const bool g_gather = S.arena_gather && all_arena && p_all_arena && !g_arena;
             const unsigned base_mask = __ballot_sync(0xffffffffu, g_base);
             const unsigned arena_mask = __ballot_sync(0xffffffffu, g_arena);
             const unsigned gather_mask = __ballot_sync(0xffffffffu, g_gather);
             const unsigned mixed_mask = ~(base_mask | arena_mask | gather_mask);
             // One 128-row box per panel when no row is remapped; the box
             // starts inside the tensor (r0 < khi <= kv_rows).
-            const bool whole_base = __all_sync(0xffffffffu, all_neg) && P.base_boxes == kBoxKinds;
+            const bool whole_base = __all_sync(0xffffffffu, all_neg) && S.base_boxes == kBoxKinds;
             // Runs: a base or arena group continues the previous group's run
             // when it is the same kind and, for arena groups, its slots follow
             // on; each run head issues power-of-two boxes for the whole run.
@@ -618,7 +529,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     int len = 1;                         // groups in this run
                     while (g + len < 16 && ((cont_mask >> (2 * (g + len))) & 1u)) ++len;
                     const CUtensorMap* mp = g_base ? base_maps : maps.a;
-                    const int kinds = g_base ? P.base_boxes : P.arena_boxes;
+                    const int kinds = g_base ? S.base_boxes : S.arena_boxes;
                     for (int off = 0; off < len;) {
                         int kind = 0;                    // largest box that fits the rest of the run
                         while (kind + 1 < kinds && (2 << kind) <= len - off) ++kind;
@@ -662,7 +573,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
                     const bool is_pad = key >= w.khi;
                     // (a padding row reads nothing; its source is any valid address)
                     const __nv_bfloat16* src = is_pad ? base
-                        : m_row >= 0 ? P.arena + (size_t)m_row * 2 * D + acol + 64 * pnl
+                        : m_row >= 0 ? S.arena + (size_t)m_row * 2 * D + acol + 64 * pnl
                                      : base + (size_t)key * D + hcol + 64 * pnl;
                     uint8_t* dst = dst_tile + pnl * kPanel;
 #pragma unroll
@@ -883,10 +794,10 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         if (P.splits > 1) {
             // partial (O, m, l) of this key chunk, fp32, for combine_splits_kernel
             const long long rr = t.row0 + row - (long long)P.q_frame0 * P.T;
-            const size_t slot = ((size_t)w.chunk * (size_t)P.ws_rows + (size_t)rr) * (size_t)P.nheads +
-                                (size_t)(w.head - P.head0);
+            const size_t slot = ((size_t)w.chunk * (size_t)P.ws_rows + (size_t)rr) * (size_t)S.nheads +
+                                (size_t)(w.head - S.head0);
             float* wo = P.ws + slot * kDH;
-            float* wml = P.ws + (size_t)P.splits * (size_t)P.ws_rows * (size_t)P.nheads * kDH + slot * 2;
+            float* wml = P.ws + (size_t)P.splits * (size_t)P.ws_rows * (size_t)S.nheads * kDH + slot * 2;
             if (t.nq > 0 && t.n_tiles > 0) {
                 if (ok && warp_wait(&sm.bar_o_done[qt], 0, sm, P.status)) {
                     tc_fence_after();
@@ -917,7 +828,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ TmaMaps maps, const __grid_consta
         } else if (ok && t.n_tiles > 0 && warp_wait(&sm.bar_o_done[qt], 0, sm, P.status)) {
             tc_fence_after();
             const float inv = 1.f / l_run;
-            __nv_bfloat16* dst = P.out + (size_t)(t.row0 + row) * D + hcol;
+            __nv_bfloat16* dst = S.out + (size_t)(t.row0 + row) * D + hcol;
 #pragma unroll
             for (int c4 = 0; c4 < 4; ++c4) {
                 uint32_t o[32];
@@ -1151,74 +1062,77 @@ int check_attn_bf16(const LayerIO& io, const AttnDesc& d) {
     return KVP_OK;
 }
 
-int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
-                     bool allow_split) {
-    const long long T = d.tokens;
+namespace {
+
+// Tensor maps and pointers of one layer (check_attn_bf16 has passed).
+int fill_seg(Seg& g, const LayerIO& io, const AttnDesc& d) {
     const int D = d.heads * kDH;
-    const int rc_check = check_attn_bf16(io, d);
-    if (rc_check != KVP_OK) return rc_check;
-    if (!d_status) {
-        set_error("attn_bf16: no status word");
-        return KVP_ERR_ARG;
-    }
-    TmaMaps maps;
-    std::memset(&maps, 0, sizeof maps);
+    std::memset(&g, 0, sizeof g);
     // Box kinds whose height fits the tensor (a box never starts past the
     // end, and a taller box than the tensor is never encoded).
     int base_boxes = 0, arena_boxes = 0;
     while (base_boxes < kBoxKinds && (8LL << base_boxes) <= io.kv_rows) ++base_boxes;
     if (io.arena)
         while (arena_boxes < kBoxKinds && (8LL << arena_boxes) <= io.arena_rows) ++arena_boxes;
-    int rc = make_map(&maps.q8, io.q, io.q_rows, D, D, 8);
+    int rc = make_map(&g.maps.q8, io.q, io.q_rows, D, D, 8);
     for (int i = 0; !rc && i < kBoxKinds; ++i) {
         const uint32_t h = 8u << (i < base_boxes ? i : 0);
-        rc = make_map(&maps.kv[0][i], io.k, io.kv_rows, D, D, h);
-        if (!rc) rc = make_map(&maps.kv[1][i], io.v, io.kv_rows, D, D, h);
+        rc = make_map(&g.maps.kv[0][i], io.k, io.kv_rows, D, D, h);
+        if (!rc) rc = make_map(&g.maps.kv[1][i], io.v, io.kv_rows, D, D, h);
         if (!rc && arena_boxes)
-            rc = make_map(&maps.a[i], io.arena, io.arena_rows, 2 * D, 2 * D, 8u << (i < arena_boxes ? i : 0));
+            rc = make_map(&g.maps.a[i], io.arena, io.arena_rows, 2 * D, 2 * D, 8u << (i < arena_boxes ? i : 0));
     }
-    if (!rc && arena_boxes) rc = make_map(&maps.a1, io.arena, io.arena_rows, 2 * D, 2 * D, 1);
+    if (!rc && arena_boxes) rc = make_map(&g.maps.a1, io.arena, io.arena_rows, 2 * D, 2 * D, 1);
     if (rc) return rc;
     if (base_boxes == 0 || io.q_rows < 8) {
         set_error("attn_bf16: Q and K/V need at least 8 rows");
         return KVP_ERR_ARG;
     }
+    g.k = (const __nv_bfloat16*)io.k;
+    g.v = (const __nv_bfloat16*)io.v;
+    g.arena = (const __nv_bfloat16*)io.arena;
+    g.kvmap = io.kvmap;
+    g.out = (__nv_bfloat16*)io.out;
+    g.q_rows = io.q_rows;
+    g.kv_rows = io.kv_rows;
+    g.arena_rows = io.arena ? io.arena_rows : 0;
+    g.D = D;
+    g.head0 = d.head0;
+    g.nheads = d.nheads;
+    g.cta0 = 0;
+    g.base_boxes = base_boxes;
+    g.arena_boxes = arena_boxes;
+    g.arena_gather = arena_boxes > 0 ? 1 : 0;
+    return KVP_OK;
+}
 
-    Params P;
+void fill_params(Params& P, const AttnDesc& d, int* d_status) {
+    const long long T = d.tokens;
     std::memset(&P, 0, sizeof P);
-    P.k = (const __nv_bfloat16*)io.k;
-    P.v = (const __nv_bfloat16*)io.v;
-    P.arena = (const __nv_bfloat16*)io.arena;
-    P.kvmap = io.kvmap;
-    P.out = (__nv_bfloat16*)io.out;
     P.status = d_status;
-    P.q_rows = io.q_rows;
-    P.kv_rows = io.kv_rows;
-    P.arena_rows = io.arena ? io.arena_rows : 0;
-    P.D = D;
     P.T = (int)T;
     P.frames = d.frames;
     P.q_frame0 = d.q_frame0;
     P.mode = d.mode;
     P.window = d.window;
-    P.head0 = d.head0;
-    P.nheads = d.nheads;
     P.flat = d.flat;
     P.n_qt = (int)((T + kBM - 1) / kBM);
     P.n_pairs = (P.n_qt + kQTiles - 1) / kQTiles;
     P.items_per_head = d.flat ? (int)(((long long)d.frames * T + kQTiles * kBM - 1) / (kQTiles * kBM))
                               : d.frames * P.n_pairs;
-    P.base_boxes = base_boxes;
-    P.arena_boxes = arena_boxes;
-    P.arena_gather = arena_boxes > 0 ? 1 : 0;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)kDH);
     P.splits = 1;
     P.ws = nullptr;
     P.ws_rows = (long long)d.frames * T;
+    P.n_segs = 1;
+}
 
+// Kernel attributes and the launch checks, once per device and instantiation.
+template <int kSegs>
+int setup_kernel() {
     const int smem = (int)sizeof(Smem);
     static PerDeviceOnce setup;
-    const int rc_setup = setup([&](int dev) -> int {
+    return setup([&](int dev) -> int {
         int optin = 0;
         KVP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
         if (smem > optin) {
@@ -1228,17 +1142,41 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
         // setmaxnreg.inc waits until the warpgroup's registers exist in the
         // CTA's pool: refuse a build whose launch pool is smaller than the split.
         cudaFuncAttributes fa;
-        KVP_CUDA(cudaFuncGetAttributes(&fa, attn_bf16_sm100_kernel));
+        KVP_CUDA(cudaFuncGetAttributes(&fa, attn_bf16_sm100_kernel<kSegs>));
         if ((long long)fa.numRegs * kThreads < (long long)kRegsLow * 128 + 2LL * kRegsHigh * 128) {
             set_error("attn_bf16: kernel built with %d registers per thread, the register split needs %d",
                       fa.numRegs, (kRegsLow * 128 + 2 * kRegsHigh * 128 + kThreads - 1) / kThreads);
             return KVP_ERR_UNSUPPORTED;
         }
-        KVP_CUDA(cudaFuncSetAttribute(attn_bf16_sm100_kernel,
+        KVP_CUDA(cudaFuncSetAttribute(attn_bf16_sm100_kernel<kSegs>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         return KVP_OK;
     });
+}
+
+}  // namespace
+
+int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
+                     bool allow_split) {
+    const long long T = d.tokens;
+    const int D = d.heads * kDH;
+    const int rc_check = check_attn_bf16(io, d);
+    if (rc_check != KVP_OK) return rc_check;
+    // KVP_ATTN_PAIR=1: the SM-pair kernel (attn_pair_sm100.cu) instead.
+    if (const char* e = std::getenv("KVP_ATTN_PAIR"))
+        if (std::atoi(e) == 1 && attn_pair_supported(d)) return launch_attn_bf16_pair(io, d, d_status, stream);
+    if (!d_status) {
+        set_error("attn_bf16: no status word");
+        return KVP_ERR_ARG;
+    }
+    SegTable<1> tab;
+    int rc = fill_seg(tab.seg[0], io, d);
+    if (rc) return rc;
+    Params P;
+    fill_params(P, d, d_status);
+    const int rc_setup = setup_kernel<1>();
     if (rc_setup != KVP_OK) return rc_setup;
+    const int smem = (int)sizeof(Smem);
     // Key-range split for per-frame launches that would leave SMs idle
     // (KVP_ATTN_SPLITS=n forces n, 1 disables).
     if (!d.flat && allow_split) {
@@ -1269,19 +1207,65 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
         if (P.ws) cudaFreeAsync(P.ws, stream);
         return KVP_ERR_ARG;
     }
-    attn_bf16_sm100_kernel<<<(unsigned)grid, kThreads, smem, stream>>>(maps, P);
+    attn_bf16_sm100_kernel<1><<<(unsigned)grid, kThreads, smem, stream>>>(tab, P);
     cudaError_t le = cudaGetLastError();
     if (P.splits > 1) {
         if (le == cudaSuccess) {
             const long long warps = P.ws_rows * d.nheads;
             combine_splits_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(
-                P.ws, P.out, P.splits, P.ws_rows, d.nheads, D, d.head0, (long long)d.q_frame0 * T);
+                P.ws, tab.seg[0].out, P.splits, P.ws_rows, d.nheads, D, d.head0, (long long)d.q_frame0 * T);
             le = cudaGetLastError();
         }
         const cudaError_t fe = cudaFreeAsync(P.ws, stream);
         if (le == cudaSuccess) le = fe;
     }
     if (le != cudaSuccess) return cuda_status(le, "attn_bf16 launch");
+    return KVP_OK;
+}
+
+int launch_attn_bf16_multi(const LayerIO* ios, const AttnDesc* ds, int n, int* d_status,
+                           cudaStream_t stream) {
+    if (!ios || !ds || n <= 0) {
+        set_error("attn_bf16_multi: no layers");
+        return KVP_ERR_ARG;
+    }
+    const AttnDesc& d0 = ds[0];
+    for (int i = 0; i < n; ++i) {
+        const AttnDesc& d = ds[i];
+        if (d.tokens != d0.tokens || d.frames != d0.frames || d.q_frame0 != d0.q_frame0 ||
+            d.mode != d0.mode || d.window != d0.window || d.flat != d0.flat) {
+            set_error("attn_bf16_multi: layer %d differs from layer 0 in tokens, frames, mode, window or tiling", i);
+            return KVP_ERR_ARG;
+        }
+        const int rc = check_attn_bf16(ios[i], d);
+        if (rc != KVP_OK) return rc;
+    }
+    if (!d_status) {
+        set_error("attn_bf16_multi: no status word");
+        return KVP_ERR_ARG;
+    }
+    const int rc_setup = setup_kernel<kMaxSegs>();
+    if (rc_setup != KVP_OK) return rc_setup;
+    const int smem = (int)sizeof(Smem);
+    Params P;
+    fill_params(P, d0, d_status);
+    SegTable<kMaxSegs> tab;
+    for (int first = 0; first < n; first += kMaxSegs) {
+        const int cnt = n - first < kMaxSegs ? n - first : kMaxSegs;
+        long long cta = 0;
+        for (int i = 0; i < cnt; ++i) {
+            const int rc = fill_seg(tab.seg[i], ios[first + i], ds[first + i]);
+            if (rc) return rc;
+            tab.seg[i].cta0 = (int)cta;
+            cta += (long long)ds[first + i].nheads * P.items_per_head;
+        }
+        for (int i = cnt; i < kMaxSegs; ++i) tab.seg[i] = tab.seg[cnt - 1];
+        P.n_segs = cnt;
+        if (cta <= 0 || cta > 0x7fffffffLL) return KVP_ERR_ARG;
+        attn_bf16_sm100_kernel<kMaxSegs><<<(unsigned)cta, kThreads, smem, stream>>>(tab, P);
+        const cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) return cuda_status(le, "attn_bf16_multi launch");
+    }
     return KVP_OK;
 }
 

@@ -51,6 +51,14 @@ struct AttnDesc {
 int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaStream_t stream,
                      bool allow_split = true);
 
+// Several layers (or head chunks) of the same shape in one launch: ios[i]
+// and ds[i] as for launch_attn_bf16; every ds[i] has the same tokens,
+// frames, q_frame0, mode, window and flat tiling, and may differ in heads,
+// head0 and nheads.  One grid over all their CTAs, so the ramp-down of a
+// short chunk overlaps the next chunk's work; no key-range split.
+int launch_attn_bf16_multi(const LayerIO* ios, const AttnDesc* ds, int n, int* d_status,
+                           cudaStream_t stream);
+
 // The launcher's argument checks alone (descriptor, row coverage, 16-byte
 // alignment), touching no device state: KVP_OK or KVP_ERR_ARG with a message.
 int check_attn_bf16(const LayerIO& io, const AttnDesc& d);

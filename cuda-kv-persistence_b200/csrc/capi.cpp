@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <vector>
 
 #include "kernels.h"
 #include "kv_tile_manager.h"
@@ -574,4 +575,26 @@ KVP_API int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* 
     int* st = kvp::status_word();
     if (!st) return kvp::KVP_ERR_CUDA;
     return kvp::launch_attn_bf16(L, A, st, (cudaStream_t)stream);
+}
+
+KVP_API int kvp_attn_bf16_multi(const kvp_layer_io* ios, const kvp_attn_desc* ds, int n,
+                                void* stream) {
+    if (!ios || !ds || n <= 0 || n > 4096) return kvp::KVP_ERR_ARG;
+    std::vector<kvp::LayerIO> L((size_t)n);
+    std::vector<kvp::AttnDesc> A((size_t)n);
+    for (int i = 0; i < n; ++i) {
+        const kvp_layer_io& io = ios[i];
+        const kvp_attn_desc& d = ds[i];
+        L[(size_t)i] = kvp::LayerIO{io.q, io.k, io.v, io.out, io.arena, io.kvmap,
+                                    io.q_rows, io.kv_rows, io.arena_rows};
+        A[(size_t)i] = kvp::AttnDesc{d.tokens, d.frames, d.q_frame0, d.mode, d.window,
+                                     d.heads, d.head_dim, d.head0, d.nheads, d.flat};
+        const int rc = kvp::check_attn_bf16(L[(size_t)i], A[(size_t)i]);
+        if (rc != kvp::KVP_OK) return rc;
+    }
+    int rc = kvp::flush_all_managers();
+    if (rc != kvp::KVP_OK) return rc;
+    int* st = kvp::status_word();
+    if (!st) return kvp::KVP_ERR_CUDA;
+    return kvp::launch_attn_bf16_multi(L.data(), A.data(), n, st, (cudaStream_t)stream);
 }

@@ -1,6 +1,8 @@
 """Attention entry points over the C ABI (torch tensors are device memory only).
 
 * ``attn_bf16``   -- tcgen05 remapped attention, one layer (kvp_attn_bf16)
+* ``attn_bf16_multi`` -- several layers / head chunks in one launch
+  (kvp_attn_bf16_multi)
 * ``attn_fp32``   -- FP32 remapped attention over a key span (kvp_attn_fp32)
 * ``attn_forward_single_frame`` / ``attn_forward_launcher`` -- the
   reference's entry points (src/attn_kernel.h:15-29), fp32
@@ -39,6 +41,30 @@ def attn_bf16(q, k, v, out, *, tokens: int, frames: int, heads: int, q_frame0: i
     d = AttnDesc(tokens, frames, q_frame0, {"intra": 0, "causal": 1, "cross": 1}[mode], window,
                  heads, 128, head0, heads - head0 if nheads is None else nheads, int(flat))
     check(lib().kvp_attn_bf16(C.byref(io), C.byref(d), C.c_void_p(_stream(stream))), "kvp_attn_bf16")
+
+
+def attn_bf16_multi(layers, *, tokens: int, frames: int, q_frame0: int = 0, mode: str = "causal",
+                    window: int = 0, flat: bool = False, stream=None) -> None:
+    """attn_bf16 over several layers or head chunks of one shape in a single
+    launch.  `layers`: dicts with q, k, v, out (bf16 [rows, h*128] tensors),
+    heads, and optionally head0, nheads, arena / arena_ptr, arena_rows,
+    kvmap / kvmap_ptr (as in attn_bf16)."""
+    n = len(layers)
+    ios = (LayerIO * n)()
+    ds = (AttnDesc * n)()
+    m = {"intra": 0, "causal": 1, "cross": 1}[mode]
+    for i, L in enumerate(layers):
+        arena, kvmap = L.get("arena"), L.get("kvmap")
+        arena_ptr, kvmap_ptr = L.get("arena_ptr", 0), L.get("kvmap_ptr", 0)
+        ios[i] = LayerIO(_ptr(L["q"]), _ptr(L["k"]), _ptr(L["v"]), _ptr(L["out"]),
+                         arena_ptr or _ptr(arena), kvmap_ptr or _ptr(kvmap), L["q"].shape[0],
+                         L["k"].shape[0],
+                         L.get("arena_rows", 0) if (arena is not None or arena_ptr) else 0)
+        heads = L["heads"]
+        head0 = L.get("head0", 0)
+        ds[i] = AttnDesc(tokens, frames, q_frame0, m, window, heads, 128, head0,
+                         L.get("nheads") or heads - head0, int(flat))
+    check(lib().kvp_attn_bf16_multi(ios, ds, n, C.c_void_p(_stream(stream))), "kvp_attn_bf16_multi")
 
 
 def attn_fp32(q, k, v, out, *, T: int, heads: int, k_lo: int, k_hi: int, arena=None,

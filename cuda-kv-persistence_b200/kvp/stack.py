@@ -16,7 +16,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .attention import attn_bf16
+from .attention import attn_bf16, attn_bf16_multi
 from .session import Session
 from .shard import chunks_of, pair_range  # noqa: F401  (pair_range re-exported)
 
@@ -113,6 +113,25 @@ class StackRank:
         else:
             attn_bf16(c.q, c.k, c.v, c.o, tokens=self.tokens, frames=self.frames,
                       heads=c.nheads, mode="causal", flat=True, stream=stream)
+
+    def attend_all(self, stream: int, group: int = 12) -> None:
+        """Every chunk, `group` chunks per launch (kvp_attn_bf16_multi): the
+        ramp-down of a short chunk overlaps the next chunk's work.  One
+        persisting window per launch, over the arena of its first chunk."""
+        for g0 in range(0, len(self.chunks), group):
+            grp = self.chunks[g0:g0 + group]
+            layers = []
+            for c in grp:
+                L = dict(q=c.q, k=c.k, v=c.v, out=c.o, heads=c.nheads)
+                if self.persist:
+                    s = self.sessions[c.session]
+                    L.update(kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(c.slot),
+                             arena_rows=s.cap_rows)
+                layers.append(L)
+            if self.persist and self.use_window:
+                self.sessions[grp[0].session].window(grp[0].slot, stream)
+            attn_bf16_multi(layers, tokens=self.tokens, frames=self.frames, mode="causal",
+                            flat=True, stream=stream)
 
     def step(self, scores, stream: int) -> None:
         self.plan_and_stage(scores, stream)

@@ -267,3 +267,27 @@ def synthetic_video(frames: int = 8, *, seed: int = 0, height: int = VIDEO_H, wi
         img = 128 + 40 * img + noise * rng.standard_normal(img.shape)
         out[f] = np.clip(np.rint(img), 0, 255).astype(np.uint8)
     return out
+
+
+def write_driver_inputs(directory, frames: int, tokens: int = TOKENS, hidden: int = HIDDEN,
+                        seed: int = 0) -> Path:
+    """Q/K/V of `frames` frames in the files the reference's driver reads
+    (src/run_policy_experiment.cu:32-43, 120-122): raw fp32
+    [frames*tokens][hidden] in q.bin, k.bin, v.bin, drawn as `qkv(...,
+    dtype=float32)`."""
+    d = Path(directory)
+    d.mkdir(parents=True, exist_ok=True)
+    for name, t in zip(("q", "k", "v"), qkv(frames * tokens, hidden, seed=seed, dtype=torch.float32)):
+        t.numpy().tofile(d / f"{name}.bin")
+    return d
+
+
+if __name__ == "__main__":
+    import argparse
+    ap = argparse.ArgumentParser(description="write the reference driver's Q/K/V input files")
+    ap.add_argument("command", choices=["driver-inputs"])
+    ap.add_argument("directory")
+    ap.add_argument("--frames", type=int, default=8)
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args()
+    print(write_driver_inputs(a.directory, a.frames, seed=a.seed))

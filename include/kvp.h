@@ -71,7 +71,10 @@ int kvp_attn_fp32(const float* q, const float* k, const float* v, const float* a
 
 /* ---- BF16 tcgen05 remapped attention (sm_100a) ---------------------------
  * Same semantics as attn_forward_kernel (src/gated_attention_kernel.cu:34-139)
- * in bf16 with fp32 accumulation, for one layer and any set of heads. */
+ * in bf16 with fp32 accumulation, for one layer and any set of heads.
+ * KVP_ATTN_PAIR=1 in the environment runs the SM-pair kernel (two CTAs per
+ * 256 query rows, tcgen05 cta_group::2) instead of the one-SM kernel; same
+ * arguments and results within the bf16 tolerance, no key-range split. */
 typedef struct {
     const void* q;          /* bf16 [q_rows][D], D = heads*128 */
     const void* k;          /* bf16 [kv_rows][D] */
@@ -96,6 +99,16 @@ typedef struct {
 } kvp_attn_desc;
 
 int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
+
+/* No counterpart in the reference (its driver launches one frame of one
+ * layer at a time, src/run_policy_experiment.cu:246-255).  kvp_attn_bf16
+ * over n layers or head chunks of the same shape in one grid: ios[i], ds[i]
+ * as for kvp_attn_bf16, all ds[i] equal in tokens, frames, q_frame0, mode,
+ * window and flat (heads / head0 / nheads may differ).  Short chunks then
+ * share their ramp-down with the next chunk's work.  Results are those of
+ * n kvp_attn_bf16 calls; no key-range split is used.  A persisting window
+ * set on `stream` covers one address range for the whole launch. */
+int kvp_attn_bf16_multi(const kvp_layer_io* ios, const kvp_attn_desc* ds, int n, void* stream);
 
 /* No counterpart in the reference.  kvp_attn_bf16 for callers that cannot
  * allocate device memory -- hosts whose allocator owns all device memory

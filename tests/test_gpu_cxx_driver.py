@@ -52,10 +52,8 @@ def _need(*exes):
 
 @pytest.fixture(scope="module")
 def inputs(tmp_path_factory, cuda):
-    d = tmp_path_factory.mktemp("drv")
-    q, k, v = (t.numpy() for t in traces.qkv(8 * T, D, seed=0, dtype=__import__("torch").float32))
-    for name, a in (("q", q), ("k", k), ("v", v)):
-        a.tofile(d / f"{name}.bin")
+    d = traces.write_driver_inputs(tmp_path_factory.mktemp("drv"), 8, seed=0)
+    q, k, v = (np.fromfile(d / f"{n}.bin", dtype=np.float32).reshape(8 * T, D) for n in "qkv")
     return d, q, k, v
 
 

@@ -33,6 +33,14 @@ def rel_l2(got, want):
     return float(np.linalg.norm((got - want).ravel()) / max(np.linalg.norm(want.ravel()), 1e-30))
 
 
+@pytest.fixture(params=["pair", "one_sm"])
+def kernel(request, monkeypatch):
+    """Both bf16 kernels: the one-SM kernel (attn_sm100.cu, the default) and
+    the SM-pair kernel (attn_pair_sm100.cu, KVP_ATTN_PAIR=1)."""
+    monkeypatch.setenv("KVP_ATTN_PAIR", "1" if request.param == "pair" else "0")
+    return request.param
+
+
 def check_bf16(got, want, what=""):
     mx, _ = errors(got, want)
     rl = rel_l2(got, want)
@@ -176,7 +184,7 @@ def _run_bf16(q, k, v, kvmap, arena, **kw):
 
 
 @pytest.mark.parametrize("T", [300, 1560])
-def test_bf16_causal_policies_bitwise(cuda, T):
+def test_bf16_causal_policies_bitwise(cuda, kernel, T):
     """Causal cross-frame, per-frame launches: none / dense / streaming /
     scattered maps give bitwise-identical outputs within tolerance of the oracle."""
     from kvp.attention import read_status
@@ -224,7 +232,7 @@ def _tile_slot_map(F, T, n_tiles, order, seed):
 
 @pytest.mark.parametrize("T", [300, 1560])
 @pytest.mark.parametrize("flat", [False, True])
-def test_bf16_tile_slots_in_any_order_bitwise(cuda, T, flat):
+def test_bf16_tile_slots_in_any_order_bitwise(cuda, kernel, T, flat):
     """Admitted tiles on descending or scattered arena slots: 8-row key
     groups wholly in the arena are fetched by TMA gather (four rows per
     instruction), groups that mix base and arena rows (frames of 300 tokens
@@ -245,7 +253,7 @@ def test_bf16_tile_slots_in_any_order_bitwise(cuda, T, flat):
         assert np.array_equal(got, none), order
 
 
-def test_bf16_flat_stack_matches_per_frame(cuda):
+def test_bf16_flat_stack_matches_per_frame(cuda, kernel):
     """Flat query tiling across frame edges (the stack layout) vs the oracle."""
     F, T, H = 4, 300, 2
     D, q, k, v = _bf16_case(F, T, H, seed=8)
@@ -260,7 +268,7 @@ def test_bf16_flat_stack_matches_per_frame(cuda):
 
 @pytest.mark.parametrize("T,mode,window", [(300, "intra", 0), (40, "intra", 0), (40, "causal", 0),
                                            (300, "causal", 2), (130, "causal", 1)])
-def test_bf16_modes_and_ragged(cuda, T, mode, window):
+def test_bf16_modes_and_ragged(cuda, kernel, T, mode, window):
     F, H = 3, 1
     D, q, k, v = _bf16_case(F, T, H, seed=10 + T)
     want = attention_frames(q, k, v, frames=F, tokens=T, heads=H, head_dim=128,
@@ -273,7 +281,7 @@ def test_bf16_modes_and_ragged(cuda, T, mode, window):
     check_bf16(a, want, (T, mode, window))
 
 
-def test_bf16_head_subset_and_frame_offset(cuda):
+def test_bf16_head_subset_and_frame_offset(cuda, kernel):
     F, T, H = 3, 300, 3
     D, q, k, v = _bf16_case(F, T, H, seed=12)
     want = attention_frames(q, k, v, frames=F, tokens=T, heads=H, head_dim=128, mode="cross")
@@ -285,7 +293,7 @@ def test_bf16_head_subset_and_frame_offset(cuda):
 
 
 @pytest.mark.parametrize("splits", ["1", "3", "7"])
-def test_bf16_key_split_matches_oracle(cuda, monkeypatch, splits):
+def test_bf16_key_split_matches_oracle(cuda, kernel, monkeypatch, splits):
     """Per-frame launches with the key range split over several CTAs (forced
     through KVP_ATTN_SPLITS; 7 leaves some chunks of the short frames empty):
     same results as the oracle, and policies stay bitwise identical."""
@@ -302,7 +310,7 @@ def test_bf16_key_split_matches_oracle(cuda, monkeypatch, splits):
 
 
 @pytest.mark.parametrize("mode,flat", [("causal", False), ("causal", True), ("intra", False)])
-def test_bf16_peaked_scores_exercise_rescale(cuda, mode, flat):
+def test_bf16_peaked_scores_exercise_rescale(cuda, kernel, mode, flat):
     """Scores with a wide, growing range: unit-scale Q, and K rows whose size
     ramps up along the key index, so a row's maximum keeps rising from tile
     to tile by more than the lazy-rescale threshold (8 in log2 units).  The
@@ -325,3 +333,46 @@ def test_bf16_peaked_scores_exercise_rescale(cuda, mode, flat):
     b = _run_bf16(q, k, v, None, None, tokens=T, frames=F, heads=H, mode=mode, flat=flat)
     assert np.array_equal(a, b)
     check_bf16(a, want, ("peaked", mode, flat))
+
+
+@pytest.mark.parametrize("flat", [True, False])
+def test_bf16_multi_layer_launch_matches_single_launches(cuda, monkeypatch, flat):
+    """kvp_attn_bf16_multi over chunks of 1 to 3 heads (14 chunks: two
+    launches of at most 12), some with a KVMap into their own arena: every
+    chunk's output is bitwise the output of its own kvp_attn_bf16 call (key
+    split off, which the multi-chunk launch never uses) and within the bf16
+    gates of the oracle."""
+    from kvp.attention import attn_bf16, attn_bf16_multi, read_status
+    monkeypatch.setenv("KVP_ATTN_SPLITS", "1")
+    F, T = 3, 300
+    mode = "causal"
+    chunks = []
+    for i in range(14):
+        h = 1 + i % 3
+        D, q, k, v = _bf16_case(F, T, h, seed=40 + i)
+        c = dict(q=_dev(q, torch.bfloat16), k=_dev(k, torch.bfloat16), v=_dev(v, torch.bfloat16),
+                 heads=h, np=(q, k, v))
+        if i % 2:
+            m = _scattered_map(F * T, 128, seed=60 + i)
+            c.update(kvmap=_dev(m), arena=_dev(build_arena(k, v, m, 128), torch.bfloat16),
+                     arena_rows=128)
+        chunks.append(c)
+    read_status()
+    for c in chunks:
+        c["out"] = torch.zeros_like(c["q"])
+    attn_bf16_multi([{kk: vv for kk, vv in c.items() if kk != "np"} for c in chunks], tokens=T,
+                    frames=F, mode=mode, flat=flat)
+    torch.cuda.synchronize()
+    assert read_status() == 0
+    for i, c in enumerate(chunks):
+        ref = torch.zeros_like(c["q"])
+        attn_bf16(c["q"], c["k"], c["v"], ref, tokens=T, frames=F, heads=c["heads"], mode=mode,
+                  flat=flat, kvmap=c.get("kvmap"), arena=c.get("arena"),
+                  arena_rows=c.get("arena_rows", 0))
+        torch.cuda.synchronize()
+        assert torch.equal(c["out"], ref), i
+        q, k, v = c["np"]
+        want = attention_frames(q, k, v, frames=F, tokens=T, heads=c["heads"], head_dim=128,
+                                mode="cross")
+        check_bf16(c["out"].float().cpu().numpy(), want, ("multi", i))
+    assert read_status() == 0
