@@ -503,9 +503,15 @@ def run_matrix(args) -> int:
     torch.cuda.set_device(0)
     if args.matrix == 5:
         for row in matrix.run_config5(reps=max(1, args.reps), seed=args.seed,
-                                      streaming=args.streaming):
+                                      streaming=args.streaming, batched=args.batched):
             print(json.dumps({"metric": "config5 cell", "streaming": args.streaming, **row}),
                   flush=True)
+    elif args.matrix == 11:
+        regimes = ("static", "high") if args.regime == "both" else (args.regime,)
+        budgets = tuple(float(x) for x in args.budgets.split(","))
+        for row in matrix.run_config5_producer(reps=max(1, args.reps), seed=args.seed,
+                                               regimes=regimes, budgets=budgets):
+            print(json.dumps({"metric": "config5 cell, K/V produced in the loop", **row}), flush=True)
     elif args.matrix == 10:
         for row in matrix.run_slot_orders(reps=max(1, args.reps) * 10, seed=args.seed):
             print(json.dumps({"metric": "one config-4 layer by arena slot order", **row}), flush=True)
@@ -528,7 +534,8 @@ def run_matrix(args) -> int:
             print(json.dumps({"metric": "config3", **row}), flush=True)
     else:
         print(json.dumps({"metric": "config2", **matrix.run_config2(reps=max(1, args.reps),
-                                                                   seed=args.seed)}), flush=True)
+                                                                   seed=args.seed,
+                                                                   batched=args.batched)}), flush=True)
     return 0
 
 
@@ -553,7 +560,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--matrix", type=int, choices=[2, 3, 5, 6, 7, 8, 9, 10], default=0,
+    ap.add_argument("--matrix", type=int, choices=[2, 3, 5, 6, 7, 8, 9, 10, 11], default=0,
                     help="instead of the config-4 line: config 5 (policy x budget x regime, one "
                          "JSON line per cell), config 3 (50 frames x 30 layers, window 5; None "
                          "and ReuseWeighted) or config 2 (one line), per-frame cross attention; "
@@ -564,8 +571,17 @@ def main() -> int:
                          "producer (GPU optical flow + tile rates) against OpenCV on the host; 9: "
                          "the attention kernel against torch SDPA backends (cuDNN first) on "
                          "intra-frame attention; 10: one config-4 layer with admitted tiles on "
-                         "ascending, descending and permuted arena slots against no map")
+                         "ascending, descending and permuted arena slots against no map; 11: "
+                         "config-5 cells (10 %% and 100 %% budgets) with the K/V produced in the "
+                         "per-frame streaming loop, so admitted rows of the current frame are "
+                         "written by the QKV epilogue instead of staged")
     ap.add_argument("--reps", type=int, default=3, help="repetitions per cell with --matrix (ABBA)")
+    ap.add_argument("--regime", choices=["static", "high", "both"], default="both",
+                    help="--matrix 11: motion regimes")
+    ap.add_argument("--budgets", default="0.1,1.0",
+                    help="--matrix 11: budget fractions of the max persisting L2, comma-separated")
+    ap.add_argument("--batched", action="store_true",
+                    help="--matrix 2/5 arena mode: plan every frame first, one grid for all frames")
     ap.add_argument("--streaming", action="store_true",
                     help="with --matrix 3 or 5: streaming arena (sticky slots, LIFO reuse) instead of "
                          "re-staging every admitted row every frame")

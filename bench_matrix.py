@@ -23,7 +23,7 @@ import numpy as np
 import torch
 
 from kvp.attention import attn_bf16, attn_bf16_multi, read_status
-from kvp.frames import run_frames, run_reuse_frames
+from kvp.frames import run_frames, run_frames_batched, run_reuse_frames
 from kvp.session import Session
 from kvp.traces import motion_config2, motion_config3, motion_config5, qkv
 
@@ -50,8 +50,14 @@ def cross_flops(frames: int, tokens: int, heads: int, head_dim: int = 128) -> fl
 
 def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: int = 12,
                 seed: int = 0, max_persist: int | None = None, streaming: bool = False,
-                device="cuda") -> list[dict]:
-    """All 40 cells, `reps` repetitions each in ABBA order; one dict per cell."""
+                device="cuda", batched: bool = False) -> list[dict]:
+    """All 40 cells, `reps` repetitions each in ABBA order; one dict per cell.
+    batched (arena mode only): every frame planned first, one grid for all
+    frames (kvp.frames.run_frames_batched)."""
+    loop = run_frames_batched if batched and not streaming else run_frames
+    extra = {} if loop is run_frames_batched else {"streaming": streaming}
+    # timed passes run the loop natively (one kvp_session_run_frames call)
+    timed_extra = extra if loop is run_frames_batched else {**extra, "native": True}
     from kvp._lib import DeviceInfo, lib
     import ctypes as C
     if max_persist is None:
@@ -72,9 +78,9 @@ def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: i
     read_status()
     # warm-up pass over every cell (also the bitwise check against None)
     for i, c in enumerate(cells):
-        counters[i] = run_frames(q, k, v, out, scores[c.regime], policy=c.policy,
-                                 set_aside=int(c.budget_frac * max_persist), frames=frames,
-                                 tokens=tokens, heads=heads, stream=stream, streaming=streaming)
+        counters[i] = loop(q, k, v, out, scores[c.regime], policy=c.policy,
+                           set_aside=int(c.budget_frac * max_persist), frames=frames,
+                           tokens=tokens, heads=heads, stream=stream, **extra)
         if c.policy == "none":
             ref.copy_(out)
         elif not torch.equal(out, ref):
@@ -87,15 +93,16 @@ def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: i
     e1 = torch.cuda.Event(enable_timing=True)
     for i in order:
         c = cells[i]
-        run_frames(q, k, v, out, scores[c.regime], policy=c.policy,
-                   set_aside=int(c.budget_frac * max_persist), frames=frames, tokens=tokens,
-                   heads=heads, stream=stream, streaming=streaming, events=(e0, e1))
+        loop(q, k, v, out, scores[c.regime], policy=c.policy,
+             set_aside=int(c.budget_frac * max_persist), frames=frames, tokens=tokens,
+             heads=heads, stream=stream, events=(e0, e1), **timed_extra)
         times[i].append(e0.elapsed_time(e1))
     status = read_status()
     res = []
     for i, c in enumerate(cells):
         t = np.array(times[i])
         res.append({"regime": c.regime, "budget_frac": c.budget_frac,
+                    "loop": "batched" if loop is run_frames_batched else ("streaming" if streaming else "arena"),
                     "set_aside_bytes": int(c.budget_frac * max_persist), "policy": c.policy,
                     "ms_mean": round(float(t.mean()), 4), "ms_std": round(float(t.std(ddof=1)) if len(t) > 1 else 0.0, 4),
                     "cv_pct": round(float(100 * t.std(ddof=1) / t.mean()) if len(t) > 1 else 0.0, 3),
@@ -106,8 +113,10 @@ def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: i
 
 
 def run_config2(*, reps: int = 3, frames: int = 8, tokens: int = 1560, heads: int = 12,
-                seed: int = 0, tiles: int = 22, device="cuda") -> dict:
-    """Config 2: 8 frames cross, AR(1) motion, Recency with 22 tiles (bf16 budget)."""
+                seed: int = 0, tiles: int = 22, device="cuda", batched: bool = False) -> dict:
+    """Config 2: 8 frames cross, AR(1) motion, Recency with 22 tiles (bf16
+    budget), arena mode; batched = one grid for all frames."""
+    loop = run_frames_batched if batched else run_frames
     hidden = heads * 128
     rows = frames * tokens
     q, k, v = (t.to(device) for t in qkv(rows, hidden, seed=seed))
@@ -116,17 +125,19 @@ def run_config2(*, reps: int = 3, frames: int = 8, tokens: int = 1560, heads: in
     scores = motion_config2(frames=frames, seed=seed)
     set_aside = tiles * 16 * hidden * 2 * 2
     read_status()
-    run_frames(q, k, v, out, scores, policy="recency", set_aside=set_aside, frames=frames,
-               tokens=tokens, heads=heads, stream=stream)
+    loop(q, k, v, out, scores, policy="recency", set_aside=set_aside, frames=frames,
+         tokens=tokens, heads=heads, stream=stream)
     ts = []
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     for _ in range(reps):
-        run_frames(q, k, v, out, scores, policy="recency", set_aside=set_aside, frames=frames,
-                   tokens=tokens, heads=heads, stream=stream, events=(e0, e1))
+        loop(q, k, v, out, scores, policy="recency", set_aside=set_aside, frames=frames,
+             tokens=tokens, heads=heads, stream=stream, events=(e0, e1),
+             **({} if batched else {"native": True}))
         ts.append(e0.elapsed_time(e1))
     t = float(np.mean(ts))
     return {"config": 2, "policy": "recency", "tiles": tiles, "frames": frames,
+            "loop": "batched" if batched else "arena",
             "ms_mean": round(t, 4), "tflops": round(cross_flops(frames, tokens, heads) / (t / 1e3) / 1e12, 2),
             "device_status": read_status()}
 
@@ -599,4 +610,106 @@ def run_slot_orders(*, reps: int = 40, warmup: int = 3, frames: int = 21, tokens
         res.append({"slots": leg, "arena_rows": legs[leg][2], "ms": round(ms, 4),
                     "tflops": round(flop / (ms / 1e3) / 1e12, 1),
                     "bitwise_eq_none": bool(torch.equal(out, ref)), "device_status": read_status()})
+    return res
+
+
+def run_config5_producer(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: int = 12,
+                         seed: int = 0, budgets=(0.10, 1.00), regimes=REGIMES,
+                         device="cuda") -> list[dict]:
+    """Config 5 cells with the K/V produced inside the per-frame loop, so the
+    rows a frame admits need no staging copy.  Per frame f, streaming mode:
+    admission (Session.plan_frame), the block's LayerNorm and QKV projection
+    of frame f's rows (kvp_session_produce: the epilogue also writes those
+    rows' K/V into their slots), a gather of only the earlier frames' newly
+    admitted rows (stage_except), the window, and the attention of frame f
+    over frames 0..f.  The None leg runs the same LayerNorm and projection
+    with no arena.  Outputs are checked bitwise against None.  One dict per
+    (regime, budget, policy); `reps` passes each, CUDA events."""
+    from kvp._lib import DeviceInfo, lib
+    from kvp.producer import layernorm, qkv_project
+    import ctypes as C
+    info = DeviceInfo()
+    lib().kvp_query_device(-1, C.byref(info))
+    max_persist = int(info.max_persisting_l2_bytes)
+    D = heads * 128
+    T = tokens
+    rows = frames * T
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(rows, D, generator=g).to(torch.bfloat16).to(device)
+    w = (0.02 * torch.randn(3 * D, D, generator=g)).to(torch.bfloat16).to(device)
+    b = (0.1 * torch.randn(3 * D, generator=g)).to(device)
+    gamma = (1 + 0.1 * torch.randn(D, generator=g)).to(device)
+    beta = (0.1 * torch.randn(D, generator=g)).to(device)
+    h = torch.empty_like(x)
+    q, k, v = (torch.empty(rows, D, dtype=torch.bfloat16, device=device) for _ in range(3))
+    out = torch.empty_like(q)
+    ref = {}
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    flops = cross_flops(frames, tokens, heads)
+    scores = {r: motion_config5(r, frames=frames, seed=seed) for r in regimes}
+
+    def one_pass(regime, budget, policy, events=None):
+        persist = policy != "none"
+        s = (Session(mode="cross", policy=policy, frames=frames, tokens=T, hidden=D, elem_bytes=2,
+                     set_aside=budget, streaming=True, layers=1) if persist else None)
+        copies = 0
+        try:
+            if events:
+                events[0].record()
+            for f in range(frames):
+                sl = slice(f * T, (f + 1) * T)
+                layernorm(x[sl], gamma, beta, h[sl], stream=stream)
+                if persist:
+                    st = s.plan_frame(f, scores[regime])
+                    copies += st.copies
+                    s.upload(stream)
+                    s.produce(0, h[sl], w, b, q[sl], k[sl], v[sl], row0=f * T, stream=stream)
+                    s.stage_except([k.data_ptr()], [v.data_ptr()], f * T, T, stream)
+                    s.window(0, stream)
+                    attn_bf16(q, k, v, out, tokens=T, frames=1, q_frame0=f, heads=heads,
+                              mode="causal", kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(0),
+                              arena_rows=s.cap_rows, stream=stream)
+                else:
+                    qkv_project(h[sl], w, b, q[sl], k[sl], v[sl], stream=stream)
+                    attn_bf16(q, k, v, out, tokens=T, frames=1, q_frame0=f, heads=heads,
+                              mode="causal", stream=stream)
+            if persist:
+                s.clear_window(stream)
+            if events:
+                events[1].record()
+            torch.cuda.synchronize()
+            if persist:
+                s.finish()
+        finally:
+            if s is not None:
+                s.close()
+        return copies
+
+    read_status()
+    res = []
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    for regime in regimes:
+        for frac in budgets:
+            budget = int(frac * max_persist)
+            for policy in POLICY_ORDER:
+                copies = one_pass(regime, budget, policy)   # warm-up and check
+                if policy == "none":
+                    ref[regime] = out.clone()
+                elif not torch.equal(out, ref[regime]):
+                    raise RuntimeError(f"producer cell {regime} {frac} {policy} differs from None")
+                ts = []
+                for _ in range(max(1, reps)):
+                    one_pass(regime, budget, policy, (e0, e1))
+                    ts.append(e0.elapsed_time(e1))
+                t = np.array(ts)
+                res.append({"regime": regime, "budget_frac": frac, "set_aside_bytes": budget,
+                            "policy": policy, "loop": "streaming+producer",
+                            "ms_mean": round(float(t.mean()), 4),
+                            "cv_pct": round(float(100 * t.std(ddof=1) / t.mean()) if len(t) > 1 else 0.0, 3),
+                            "attention_tflops": round(flops / (t.mean() / 1e3) / 1e12, 2),
+                            "staging_copies_per_pass": copies, "reps": len(t)})
+    status = read_status()
+    for r in res:
+        r["device_status"] = status
     return res

@@ -115,7 +115,7 @@ struct Seg {
     const long long* kvmap;
     __nv_bfloat16* out;
     long long q_rows, kv_rows, arena_rows;
-    int D, head0, nheads, cta0;
+    int D, head0, nheads, cta0, q_frame0;
     int base_boxes, arena_boxes;   // box kinds usable (heights <= tensor rows); 0 = no arena TMA
     int arena_gather;              // 1 = maps.a1 is encoded (scattered arena groups by TMA gather)
 };
@@ -130,12 +130,13 @@ struct SegHot {
     const long long* kvmap;
     __nv_bfloat16* out;
     long long q_rows, kv_rows, arena_rows;
-    int D, head0, nheads, cta0, base_boxes, arena_boxes, arena_gather;
+    int D, head0, nheads, cta0, q_frame0, base_boxes, arena_boxes, arena_gather;
 };
 
 __device__ __forceinline__ SegHot seg_hot(const Seg& g) {
     return SegHot{g.k, g.v, g.arena, g.kvmap, g.out, g.q_rows, g.kv_rows, g.arena_rows,
-                  g.D, g.head0, g.nheads, g.cta0, g.base_boxes, g.arena_boxes, g.arena_gather};
+                  g.D, g.head0, g.nheads, g.cta0, g.q_frame0, g.base_boxes, g.arena_boxes,
+                  g.arena_gather};
 }
 
 // Segments per launch: 1 for kvp_attn_bf16, up to kMaxSegs for
@@ -151,7 +152,7 @@ struct SegTable {
 // split workspace, the status word.
 struct Params {
     int* status;
-    int T, frames, q_frame0, mode, window, flat, items_per_head, n_qt, n_pairs, n_segs;
+    int T, frames, mode, window, flat, items_per_head, n_qt, n_pairs, n_segs;
     float scale_log2;
     // Key-range split (per-frame tiling only): splits > 1 writes fp32 partial
     // (O, m, l) to ws instead of bf16 output; combine_splits_kernel merges.
@@ -263,8 +264,8 @@ __device__ __forceinline__ Work decode_work(const Params& P, const SegHot& S) {
     w.chunk = 0;
     const long long T = P.T;
     if (P.flat) {
-        const long long R0 = (long long)P.q_frame0 * T;
-        const long long R1 = (long long)(P.q_frame0 + P.frames) * T;
+        const long long R0 = (long long)S.q_frame0 * T;
+        const long long R1 = (long long)(S.q_frame0 + P.frames) * T;
         const long long t = (long long)(P.items_per_head - 1 - i);  // longest first
         w.klo = 0;
 #pragma unroll
@@ -287,7 +288,7 @@ __device__ __forceinline__ Work decode_work(const Params& P, const SegHot& S) {
         w.chunk = i % P.splits;
         const int ip = i / P.splits;
         const int fr = ip / P.n_pairs, pr = ip % P.n_pairs;
-        const int f = P.q_frame0 + P.frames - 1 - fr;  // longest key span first
+        const int f = S.q_frame0 + P.frames - 1 - fr;  // longest key span first
         if (P.mode == 0) {
             w.klo = (long long)f * T;
         } else {
@@ -793,7 +794,7 @@ attn_bf16_sm100_kernel(const __grid_constant__ SegTable<kSegs> tab, const __grid
         }
         if (P.splits > 1) {
             // partial (O, m, l) of this key chunk, fp32, for combine_splits_kernel
-            const long long rr = t.row0 + row - (long long)P.q_frame0 * P.T;
+            const long long rr = t.row0 + row - (long long)S.q_frame0 * P.T;
             const size_t slot = ((size_t)w.chunk * (size_t)P.ws_rows + (size_t)rr) * (size_t)S.nheads +
                                 (size_t)(w.head - S.head0);
             float* wo = P.ws + slot * kDH;
@@ -1100,6 +1101,7 @@ int fill_seg(Seg& g, const LayerIO& io, const AttnDesc& d) {
     g.head0 = d.head0;
     g.nheads = d.nheads;
     g.cta0 = 0;
+    g.q_frame0 = d.q_frame0;
     g.base_boxes = base_boxes;
     g.arena_boxes = arena_boxes;
     g.arena_gather = arena_boxes > 0 ? 1 : 0;
@@ -1112,7 +1114,6 @@ void fill_params(Params& P, const AttnDesc& d, int* d_status) {
     P.status = d_status;
     P.T = (int)T;
     P.frames = d.frames;
-    P.q_frame0 = d.q_frame0;
     P.mode = d.mode;
     P.window = d.window;
     P.flat = d.flat;
@@ -1232,8 +1233,8 @@ int launch_attn_bf16_multi(const LayerIO* ios, const AttnDesc* ds, int n, int* d
     const AttnDesc& d0 = ds[0];
     for (int i = 0; i < n; ++i) {
         const AttnDesc& d = ds[i];
-        if (d.tokens != d0.tokens || d.frames != d0.frames || d.q_frame0 != d0.q_frame0 ||
-            d.mode != d0.mode || d.window != d0.window || d.flat != d0.flat) {
+        if (d.tokens != d0.tokens || d.frames != d0.frames || d.mode != d0.mode ||
+            d.window != d0.window || d.flat != d0.flat) {
             set_error("attn_bf16_multi: layer %d differs from layer 0 in tokens, frames, mode, window or tiling", i);
             return KVP_ERR_ARG;
         }

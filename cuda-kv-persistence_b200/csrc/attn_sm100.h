@@ -53,8 +53,9 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
 
 // Several layers (or head chunks) of the same shape in one launch: ios[i]
 // and ds[i] as for launch_attn_bf16; every ds[i] has the same tokens,
-// frames, q_frame0, mode, window and flat tiling, and may differ in heads,
-// head0 and nheads.  One grid over all their CTAs, so the ramp-down of a
+// frames, mode, window and flat tiling, and may differ in heads, head0,
+// nheads and q_frame0 (e.g. consecutive frames of one layer, each with the
+// KVMap and arena its admission step produced).  One grid over all their CTAs, so the ramp-down of a
 // short chunk overlaps the next chunk's work; no key-range split.
 int launch_attn_bf16_multi(const LayerIO* ios, const AttnDesc* ds, int n, int* d_status,
                            cudaStream_t stream);

@@ -598,3 +598,36 @@ KVP_API int kvp_attn_bf16_multi(const kvp_layer_io* ios, const kvp_attn_desc* ds
     if (!st) return kvp::KVP_ERR_CUDA;
     return kvp::launch_attn_bf16_multi(L.data(), A.data(), n, st, (cudaStream_t)stream);
 }
+
+// The per-frame loop (kvp.h); Session::step, then the attention of the frame.
+KVP_API int kvp_session_run_frames(void* sp, int f0, int nframes, const float* scores_flat,
+                                   const signed char* reuse_flat, const kvp_layer_io* io,
+                                   const kvp_attn_desc* d, void* stream) {
+    auto* s = static_cast<kvp::Session*>(sp);
+    if (!s || !io || !d || nframes <= 0 || f0 < 0) return kvp::KVP_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    kvp::LayerIO L{io->q, io->k, io->v, io->out, nullptr, nullptr, io->q_rows, io->kv_rows, 0};
+    kvp::AttnDesc A{d->tokens, 1, f0, d->mode, d->window, d->heads, d->head_dim, d->head0,
+                    d->nheads, 0};
+    const bool persist = s->persists();
+    if (persist) {
+        L.kvmap = reinterpret_cast<const long long*>(s->device_map());
+        L.arena = s->arena(0);
+        L.arena_rows = s->cap_rows();
+    }
+    // Bad arguments are reported before any device work.
+    int rc = kvp::check_attn_bf16(L, A);
+    if (rc != kvp::KVP_OK) return rc;
+    int* status = kvp::status_word();
+    if (!status) return kvp::KVP_ERR_CUDA;
+    const void* kl[1] = {io->k};
+    const void* vl[1] = {io->v};
+    for (int f = f0; f < f0 + nframes; ++f) {
+        rc = s->step(f, scores_flat, reinterpret_cast<const int8_t*>(reuse_flat), kl, vl, 0, st);
+        if (rc != kvp::KVP_OK) return rc;
+        A.q_frame0 = f;
+        rc = kvp::launch_attn_bf16(L, A, status, st);
+        if (rc != kvp::KVP_OK) return rc;
+    }
+    return persist ? s->clear_window(st) : kvp::KVP_OK;
+}

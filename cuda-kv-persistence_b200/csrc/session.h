@@ -83,6 +83,7 @@ public:
     const std::vector<int32_t>& pairs() const { return pairs_; }  // (row, slot) interleaved
     const std::vector<long>& selected_ids() const { return sel_ids_; }
     int64_t slots() const { return slots_; }
+    bool persists() const { return c_.policy != POLICY_NONE; }
     int64_t cap_rows() const { return cap_rows_; }
     int64_t map_len() const { return (int64_t)map_.size(); }
     int finish();  // streaming_end / final demote (same as the driver's end of run)

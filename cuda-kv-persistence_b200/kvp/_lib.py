@@ -126,6 +126,8 @@ SIGNATURES = {
                                 C.c_longlong, C.c_longlong, C.c_void_p]),
     "kvp_attn_bf16": (C.c_int, [C.POINTER(LayerIO), C.POINTER(AttnDesc), C.c_void_p]),
     "kvp_attn_bf16_multi": (C.c_int, [C.POINTER(LayerIO), C.POINTER(AttnDesc), C.c_int, C.c_void_p]),
+    "kvp_session_run_frames": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                         C.POINTER(LayerIO), C.POINTER(AttnDesc), C.c_void_p]),
     "kvp_attn_bf16_noalloc": (C.c_int, [C.POINTER(LayerIO), C.POINTER(AttnDesc), C.c_void_p,
                                         C.POINTER(C.c_int), C.c_void_p]),
     "kvp_session_create": (C.c_void_p, [C.POINTER(SessionConfig)]),

@@ -47,8 +47,8 @@ def attn_bf16_multi(layers, *, tokens: int, frames: int, q_frame0: int = 0, mode
                     window: int = 0, flat: bool = False, stream=None) -> None:
     """attn_bf16 over several layers or head chunks of one shape in a single
     launch.  `layers`: dicts with q, k, v, out (bf16 [rows, h*128] tensors),
-    heads, and optionally head0, nheads, arena / arena_ptr, arena_rows,
-    kvmap / kvmap_ptr (as in attn_bf16)."""
+    heads, and optionally head0, nheads, q_frame0, arena / arena_ptr,
+    arena_rows, kvmap / kvmap_ptr (as in attn_bf16)."""
     n = len(layers)
     ios = (LayerIO * n)()
     ds = (AttnDesc * n)()
@@ -62,7 +62,7 @@ def attn_bf16_multi(layers, *, tokens: int, frames: int, q_frame0: int = 0, mode
                          L.get("arena_rows", 0) if (arena is not None or arena_ptr) else 0)
         heads = L["heads"]
         head0 = L.get("head0", 0)
-        ds[i] = AttnDesc(tokens, frames, q_frame0, m, window, heads, 128, head0,
+        ds[i] = AttnDesc(tokens, frames, L.get("q_frame0", q_frame0), m, window, heads, 128, head0,
                          L.get("nheads") or heads - head0, int(flat))
     check(lib().kvp_attn_bf16_multi(ios, ds, n, C.c_void_p(_stream(stream))), "kvp_attn_bf16_multi")
 

@@ -144,6 +144,25 @@ class Session:
                                        None if r is None else r.ctypes.data, ka, va, window_layer,
                                        C.c_void_p(stream)), "step")
 
+    def run_frames(self, f0: int, nframes: int, scores_flat: np.ndarray, q, k, v, out, *,
+                   heads: int, mode: str = "causal", window: int = 0, reuse=None,
+                   stream: int = 0):
+        """The per-frame loop of one layer in one native call
+        (kvp_session_run_frames): step(f) then the attention of query frame f
+        through this step's KVMap and arena 0, for f in [f0, f0 + nframes)."""
+        from ._lib import AttnDesc, LayerIO
+        sflat = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
+        r = None
+        if reuse is not None and self.mode == "reuse":
+            r = np.ascontiguousarray(reuse, dtype=np.int8).reshape(-1)
+        io = LayerIO(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), 0, 0, q.shape[0],
+                     k.shape[0], 0)
+        d = AttnDesc(self.tokens, 1, f0, {"intra": 0, "causal": 1}[mode], window, heads, 128, 0,
+                     heads, 0)
+        check(self._L.kvp_session_run_frames(self.h, f0, nframes, sflat.ctypes.data,
+                                             None if r is None else r.ctypes.data, C.byref(io),
+                                             C.byref(d), C.c_void_p(stream)), "run_frames")
+
     def stage_except(self, k_ptrs, v_ptrs, skip_row0: int, skip_rows: int, stream: int = 0):
         """stage() without the source rows [skip_row0, skip_row0 + skip_rows)."""
         n = len(k_ptrs)

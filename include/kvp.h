@@ -102,9 +102,9 @@ int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
 
 /* No counterpart in the reference (its driver launches one frame of one
  * layer at a time, src/run_policy_experiment.cu:246-255).  kvp_attn_bf16
- * over n layers or head chunks of the same shape in one grid: ios[i], ds[i]
- * as for kvp_attn_bf16, all ds[i] equal in tokens, frames, q_frame0, mode,
- * window and flat (heads / head0 / nheads may differ).  Short chunks then
+ * over n layers, head chunks or query frames in one grid: ios[i], ds[i] as
+ * for kvp_attn_bf16, all ds[i] equal in tokens, frames, mode, window and
+ * flat (heads / head0 / nheads / q_frame0 may differ).  Short chunks then
  * share their ramp-down with the next chunk's work.  Results are those of
  * n kvp_attn_bf16 calls; no key-range split is used.  A persisting window
  * set on `stream` covers one address range for the whole launch. */
@@ -259,6 +259,19 @@ int kvp_session_produce(void* s, int layer, const void* x, const void* w, const 
 int kvp_session_step(void* s, int frame, const float* scores_flat, const signed char* reuse_flat,
                      const void* const* k_layers, const void* const* v_layers, int window_layer,
                      void* stream);
+/* The per-frame loop of one layer in one call, no reference counterpart
+ * (the reference driver runs it inline, src/run_policy_experiment.cu:156-274,
+ * with a device synchronisation per frame): for f in [f0, f0 + nframes),
+ * kvp_session_step(f, scores_flat, reuse_flat, &io->k, &io->v, window 0),
+ * then kvp_attn_bf16 of query frame f (*d with q_frame0 = f, frames = 1)
+ * through this step's KVMap and arena 0 (no map for the None policy);
+ * finally the persisting window is cleared.  Everything is queued on
+ * `stream`; the host plans frame f+1 while the device runs frame f.
+ * io->arena / io->kvmap / io->arena_rows are ignored.  Stops at the first
+ * error and returns it. */
+int kvp_session_run_frames(void* s, int f0, int nframes, const float* scores_flat,
+                           const signed char* reuse_flat, const kvp_layer_io* io,
+                           const kvp_attn_desc* d, void* stream);
 
 #ifdef __cplusplus
 }

@@ -114,3 +114,57 @@ def test_config5_full_budget(inputs16, oracle16, regime, streaming):
                          ("none", "uniform", "recency", "motion", "reuse_weighted"),
                          set_aside=_max_persist(), frames=16, streaming=streaming)
     _check(outs, oracle16, ("config 5", regime, streaming))
+
+
+@pytest.mark.parametrize("config", ["2", "5-high"])
+def test_batched_frames_match_the_per_frame_loop(inputs16, oracle16, monkeypatch, config):
+    """Arena mode with every frame planned first, staged into an arena of its
+    own and run in one grid (kvp.frames.run_frames_batched): each policy's
+    output is bitwise the per-frame loop's (key split off, which the batched
+    grid never uses), bitwise None's, and within the bf16 gates."""
+    from kvp.attention import read_status
+    from kvp.frames import run_frames, run_frames_batched
+    monkeypatch.setenv("KVP_ATTN_SPLITS", "1")
+    if config == "2":
+        F, policies, budget = 8, ("none", "recency"), 2162688
+        scores = read_motion_csv(GOLDEN / "motion_config2.csv", 8, TILES)
+    else:
+        F, policies, budget = 16, ("none", "uniform", "recency", "motion", "reuse_weighted"), _max_persist()
+        scores = read_motion_csv(GOLDEN / "motion_config5_high.csv", 16, TILES)
+    q, k, v = (t[:F * T] for t in inputs16)
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    read_status()
+    outs = {}
+    for policy in policies:
+        a = torch.full_like(q, float("nan"))
+        b = torch.full_like(q, float("nan"))
+        run_frames_batched(q, k, v, a, scores, policy=policy, set_aside=budget, frames=F, tokens=T,
+                           heads=H, stream=stream)
+        run_frames(q, k, v, b, scores, policy=policy, set_aside=budget, frames=F, tokens=T,
+                   heads=H, stream=stream)
+        assert torch.equal(a, b), policy
+        outs[policy] = a.float().cpu().numpy()
+    assert read_status() == 0
+    want = oracle16 if F == 16 else _oracle_heads(q, k, v, F)
+    _check(outs, want[:F * T], ("batched", config))
+
+
+@pytest.mark.parametrize("streaming", [False, True], ids=["arena", "streaming"])
+def test_native_loop_matches_the_python_loop(inputs16, streaming):
+    """kvp_session_run_frames (the whole per-frame loop in one native call)
+    gives the bytes of the step-by-step loop, config 5 high at 10 %."""
+    from kvp.attention import read_status
+    from kvp.frames import run_frames
+    scores = read_motion_csv(GOLDEN / "motion_config5_high.csv", 16, TILES)
+    q, k, v = inputs16
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    read_status()
+    for policy in ("none", "reuse_weighted", "recency"):
+        a = torch.full_like(q, float("nan"))
+        b = torch.full_like(q, float("nan"))
+        kw = dict(policy=policy, set_aside=_max_persist() // 10, frames=16, tokens=T, heads=H,
+                  stream=stream, streaming=streaming)
+        run_frames(q, k, v, a, scores, native=True, **kw)
+        run_frames(q, k, v, b, scores, **kw)
+        assert torch.equal(a, b), policy
+    assert read_status() == 0
