@@ -68,15 +68,23 @@ def measured_peaks():
     return 1400.0, 6650.0, "fallback"
 
 
-def profiled_traffic(kernel: str):
-    """dram read+write bytes per attention launch of `kernel` from the
-    committed ncu summary of one stack layer (profiles/*stack21*.md)."""
+def profiled_traffic_per_layer(kernel: str):
+    """DRAM read + write bytes per stack layer of `kernel`'s attention, from
+    the committed ncu summaries of stack layers (profiles/*stack21*.md): a
+    `traffic_bytes_per_layer` line, else a one-layer launch's
+    `traffic_bytes_per_launch`."""
+    best = None
     for p in sorted((ROOT / "profiles").glob("*stack21*.md")):
         text = p.read_text()
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", text)
-        if m and kernel in text:
+        if kernel not in text:
+            continue
+        m = re.search(r"traffic_bytes_per_layer:\s*([0-9.eE+]+)", text)
+        if m:
             return float(m.group(1))
-    return None
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", text)
+        if m and best is None:
+            best = float(m.group(1))
+    return best
 
 
 def profiled_dram_per_step():
@@ -355,10 +363,15 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
         local_attn_flops = stack.flops() * args.steps
         achieved = local_attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms > 0 else None
         per_launch_flops = local_attn_flops / max(n_attn, 1)
+        traffic_layer = profiled_traffic_per_layer(attention_kernel())
+        layers_per_event = stack.n_pairs / HEADS * args.steps / max(n_attn, 1)
         roofline = {"bound": "tensor", "achieved": round(achieved, 2) if achieved else None,
                     "peak": peak, "unit": "TFLOP/s",
                     "frac": round(achieved / peak, 4) if achieved else None,
-                    "traffic": profiled_traffic(attention_kernel()), "kernel": attention_kernel(),
+                    "traffic": (round(traffic_layer * layers_per_event) if traffic_layer else None),
+                    "traffic_unit": "DRAM bytes per timed attention unit (the step's attention "
+                                    "launches on this rank), from the per-layer ncu figure",
+                    "kernel": attention_kernel(),
                     "peak_kind": f"{peak_kind} bf16 sustained (cuBLAS)",
                     "flop_per_launch": per_launch_flops,
                     "avg_launch_ms": round(attn_ms / max(n_attn, 1), 4)}
