@@ -259,8 +259,12 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
             c.o = buf[off:off + n].view(c.o.shape)
             off += n
 
-    attn_launches = (-(-len(stack.chunks) // args.group) if args.launch == "multi"
-                     else len(stack.chunks))
+    if args.launch == "multi":
+        per_call = args.group if args.group > 0 else len(stack.chunks)
+        attn_launches = sum(-(-min(per_call, len(stack.chunks) - g0) // 12)
+                            for g0 in range(0, len(stack.chunks), per_call))
+    else:
+        attn_launches = len(stack.chunks)
     launches_per_step = attn_launches + (len(stack.sessions) if stack.persist else 0)
     attn_events = []
     gather_done = [None, None]   # last all-gather that read each output buffer
@@ -569,7 +573,9 @@ def main() -> int:
     ap.add_argument("--launch", choices=["multi", "layer"], default="multi",
                     help="attention launches: several layer chunks per launch (kvp_attn_bf16_multi) "
                          "or one per layer chunk (kvp_attn_bf16)")
-    ap.add_argument("--group", type=int, default=12, help="layer chunks per launch with --launch multi")
+    ap.add_argument("--group", type=int, default=0,
+                    help="layer chunks per kvp_attn_bf16_multi call with --launch multi (0 = all; "
+                         "the library then spreads them evenly over launches of at most 12)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

@@ -158,8 +158,9 @@ def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: i
     frame f over key frames max(0, f-window+1)..f in every layer: launch
     "layer" sets each layer's persisting window over its arena and launches
     that layer alone (the reference driver's structure); launch "multi" runs
-    the layers 12 to a launch (kvp_attn_bf16_multi) under one window over the
-    first layer's arena.  Also the None policy on the same inputs."""
+    every layer through one kvp_attn_bf16_multi call (10 layers a launch)
+    under one window over the first layer's arena.  Also the None policy on
+    the same inputs."""
     from kvp._lib import DeviceInfo, lib
     import ctypes as C
     info = DeviceInfo()
@@ -198,11 +199,10 @@ def run_config3(*, reps: int = 2, frames: int = 50, tokens: int = 1560, heads: i
                             L.update(kvmap_ptr=s.device_map_ptr(), arena_ptr=s.arena_ptr(layer),
                                      arena_rows=s.cap_rows)
                         group.append(L)
-                    for g0 in range(0, layers, 12):
-                        if persist:
-                            s.window(g0, stream)
-                        attn_bf16_multi(group[g0:g0 + 12], tokens=tokens, frames=1, q_frame0=f,
-                                        mode="causal", window=window, stream=stream)
+                    if persist:
+                        s.window(0, stream)
+                    attn_bf16_multi(group, tokens=tokens, frames=1, q_frame0=f, mode="causal",
+                                    window=window, stream=stream)
                     continue
                 for layer in range(layers):
                     if persist:

@@ -1251,8 +1251,12 @@ int launch_attn_bf16_multi(const LayerIO* ios, const AttnDesc* ds, int n, int* d
     Params P;
     fill_params(P, d0, d_status);
     SegTable<kMaxSegs> tab;
-    for (int first = 0; first < n; first += kMaxSegs) {
-        const int cnt = n - first < kMaxSegs ? n - first : kMaxSegs;
+    // As few launches as the table allows, with the segments spread evenly
+    // over them (30 layers: 10 + 10 + 10, not 12 + 12 + 6).
+    const int launches = (n + kMaxSegs - 1) / kMaxSegs;
+    const int per_launch = (n + launches - 1) / launches;
+    for (int first = 0; first < n; first += per_launch) {
+        const int cnt = n - first < per_launch ? n - first : per_launch;
         long long cta = 0;
         for (int i = 0; i < cnt; ++i) {
             const int rc = fill_seg(tab.seg[i], ios[first + i], ds[first + i]);

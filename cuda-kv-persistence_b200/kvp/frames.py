@@ -158,9 +158,7 @@ def run_frames_batched(q, k, v, out, scores, *, policy: str, set_aside: int, fra
             layers.append(L)
         if persist:
             s.window(frames - 1, stream)
-        for g0 in range(0, frames, 12):
-            attn_bf16_multi(layers[g0:g0 + 12], tokens=tokens, frames=1, mode=amode, window=win,
-                            stream=stream)
+        attn_bf16_multi(layers, tokens=tokens, frames=1, mode=amode, window=win, stream=stream)
         if persist:
             s.clear_window(stream)
         if events:

@@ -114,12 +114,15 @@ class StackRank:
             attn_bf16(c.q, c.k, c.v, c.o, tokens=self.tokens, frames=self.frames,
                       heads=c.nheads, mode="causal", flat=True, stream=stream)
 
-    def attend_all(self, stream: int, group: int = 12) -> None:
-        """Every chunk, `group` chunks per launch (kvp_attn_bf16_multi): the
-        ramp-down of a short chunk overlaps the next chunk's work.  One
-        persisting window per launch, over the arena of its first chunk."""
-        for g0 in range(0, len(self.chunks), group):
-            grp = self.chunks[g0:g0 + group]
+    def attend_all(self, stream: int, group: int = 0) -> None:
+        """Every chunk through kvp_attn_bf16_multi: the ramp-down of a short
+        chunk overlaps the next chunk's work.  group = 0 passes all chunks in
+        one call (the library spreads them evenly over as few launches as its
+        segment table allows); group > 0 makes one call per `group` chunks.
+        One persisting window per call, over the arena of its first chunk."""
+        step = group if group > 0 else len(self.chunks)
+        for g0 in range(0, len(self.chunks), step):
+            grp = self.chunks[g0:g0 + step]
             layers = []
             for c in grp:
                 L = dict(q=c.q, k=c.k, v=c.v, out=c.o, heads=c.nheads)

@@ -105,7 +105,8 @@ int kvp_attn_bf16(const kvp_layer_io* io, const kvp_attn_desc* d, void* stream);
  * over n layers, head chunks or query frames in one grid: ios[i], ds[i] as
  * for kvp_attn_bf16, all ds[i] equal in tokens, frames, mode, window and
  * flat (heads / head0 / nheads / q_frame0 may differ).  Short chunks then
- * share their ramp-down with the next chunk's work.  Results are those of
+ * share their ramp-down with the next chunk's work.  A launch holds up to 12
+ * of them; more are spread evenly over as few launches as needed.  Results are those of
  * n kvp_attn_bf16 calls; no key-range split is used.  A persisting window
  * set on `stream` covers one address range for the whole launch. */
 int kvp_attn_bf16_multi(const kvp_layer_io* ios, const kvp_attn_desc* ds, int n, void* stream);
