@@ -591,7 +591,14 @@ KVP_API int kvp_attn_bf16_multi(const kvp_layer_io* ios, const kvp_attn_desc* ds
                                      d.heads, d.head_dim, d.head0, d.nheads, d.flat};
         const int rc = kvp::check_attn_bf16(L[(size_t)i], A[(size_t)i]);
         if (rc != kvp::KVP_OK) return rc;
+        if (d.tokens != ds[0].tokens || d.frames != ds[0].frames || d.mode != ds[0].mode ||
+            d.window != ds[0].window || d.flat != ds[0].flat) {
+            kvp::set_error("attn_bf16_multi: layer %d differs from layer 0 in tokens, frames, mode, "
+                           "window or tiling", i);
+            return kvp::KVP_ERR_ARG;
+        }
     }
+    // Bad arguments are reported above, before any device work.
     int rc = kvp::flush_all_managers();
     if (rc != kvp::KVP_OK) return rc;
     int* st = kvp::status_word();

@@ -181,3 +181,43 @@ def test_attn_bf16_noalloc_rejects_before_touching_the_device():
                                                                           0, 2, 0)),
                                      None, None, None)
     assert rc == ERR_ARG
+
+
+def test_attn_bf16_multi_rejects_before_touching_the_device():
+    """kvp_attn_bf16_multi checks every layer's descriptor and that the
+    layers share tokens, frames, mode, window and tiling, before any device
+    work; q_frame0 and the head range may differ."""
+    io = LayerIO(0x10000, 0x20000, 0x30000, 0x40000, 0, 0, 900, 900, 0)
+    ios = (LayerIO * 2)(io, io)
+    good = AttnDesc(300, 1, 0, 1, 0, 2, 128, 0, 2, 0)
+    for other in (AttnDesc(301, 1, 0, 1, 0, 2, 128, 0, 2, 0),    # tokens
+                  AttnDesc(300, 2, 0, 1, 0, 2, 128, 0, 2, 0),    # frames
+                  AttnDesc(300, 1, 0, 0, 0, 2, 128, 0, 2, 0),    # mode
+                  AttnDesc(300, 1, 0, 1, 2, 2, 128, 0, 2, 0)):   # window
+        ds = (AttnDesc * 2)(good, other)
+        assert lib().kvp_attn_bf16_multi(ios, ds, 2, None) == ERR_ARG
+        assert b"differs from layer 0" in lib().kvp_last_error()
+    bad = (AttnDesc * 2)(good, AttnDesc(300, 1, 0, 1, 0, 2, 64, 0, 2, 0))   # head_dim 64
+    assert lib().kvp_attn_bf16_multi(ios, bad, 2, None) == ERR_ARG
+    assert lib().kvp_attn_bf16_multi(ios, (AttnDesc * 2)(good, good), 0, None) == ERR_ARG
+
+
+def test_session_run_frames_rejects_bad_arguments():
+    """kvp_session_run_frames refuses a missing session, descriptor or frame
+    range, and a bad descriptor, before any device work."""
+    from kvp.session import Session
+    s = Session(mode="cross", policy="none", frames=2, tokens=300, hidden=256, elem_bytes=2,
+                set_aside=0, layers=0)
+    try:
+        io = LayerIO(0x10000, 0x20000, 0x30000, 0x40000, 0, 0, 600, 600, 0)
+        d = AttnDesc(300, 1, 0, 1, 0, 2, 128, 0, 2, 0)
+        scores = np.zeros(2 * 19, dtype=np.float32)
+        f = lib().kvp_session_run_frames
+        assert f(None, 0, 2, scores.ctypes.data, None, C.byref(io), C.byref(d), None) == ERR_ARG
+        assert f(s.h, 0, 0, scores.ctypes.data, None, C.byref(io), C.byref(d), None) == ERR_ARG
+        assert f(s.h, -1, 2, scores.ctypes.data, None, C.byref(io), C.byref(d), None) == ERR_ARG
+        assert f(s.h, 0, 2, scores.ctypes.data, None, None, C.byref(d), None) == ERR_ARG
+        d64 = AttnDesc(300, 1, 0, 1, 0, 2, 64, 0, 2, 0)
+        assert f(s.h, 0, 2, scores.ctypes.data, None, C.byref(io), C.byref(d64), None) == ERR_ARG
+    finally:
+        s.close()
