@@ -622,7 +622,9 @@ KVP_API int kvp_session_run_frames(void* sp, int f0, int nframes, const float* s
         L.arena = s->arena(0);
         L.arena_rows = s->cap_rows();
     }
-    // Bad arguments are reported before any device work.
+    // Bad arguments are reported before any device work; the last frame's
+    // rows bound every earlier frame's.
+    A.q_frame0 = f0 + nframes - 1;
     int rc = kvp::check_attn_bf16(L, A);
     if (rc != kvp::KVP_OK) return rc;
     int* status = kvp::status_word();

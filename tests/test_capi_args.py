@@ -217,6 +217,8 @@ def test_session_run_frames_rejects_bad_arguments():
         assert f(s.h, 0, 0, scores.ctypes.data, None, C.byref(io), C.byref(d), None) == ERR_ARG
         assert f(s.h, -1, 2, scores.ctypes.data, None, C.byref(io), C.byref(d), None) == ERR_ARG
         assert f(s.h, 0, 2, scores.ctypes.data, None, None, C.byref(d), None) == ERR_ARG
+        # 3 frames of 300 rows do not fit the 600 rows the buffers hold
+        assert f(s.h, 0, 3, scores.ctypes.data, None, C.byref(io), C.byref(d), None) == ERR_ARG
         d64 = AttnDesc(300, 1, 0, 1, 0, 2, 64, 0, 2, 0)
         assert f(s.h, 0, 2, scores.ctypes.data, None, C.byref(io), C.byref(d64), None) == ERR_ARG
     finally:
