@@ -550,9 +550,12 @@ def run_matrix(args) -> int:
                                       streaming=args.streaming, launch=args.launch):
             print(json.dumps({"metric": "config3", **row}), flush=True)
     else:
-        print(json.dumps({"metric": "config2", **matrix.run_config2(reps=max(1, args.reps),
-                                                                   seed=args.seed,
-                                                                   batched=args.batched)}), flush=True)
+        # the per-frame loop, then all frames in one grid (--batched: that alone)
+        for batched in ((True,) if args.batched else (False, True)):
+            print(json.dumps({"metric": "config2", **matrix.run_config2(reps=max(1, args.reps),
+                                                                       seed=args.seed,
+                                                                       batched=batched)}),
+                  flush=True)
     return 0
 
 
@@ -600,7 +603,9 @@ def main() -> int:
     ap.add_argument("--budgets", default="0.1,1.0",
                     help="--matrix 11: budget fractions of the max persisting L2, comma-separated")
     ap.add_argument("--batched", action="store_true",
-                    help="--matrix 2/5 arena mode: plan every frame first, one grid for all frames")
+                    help="--matrix 2/5 arena mode: plan every frame first, one grid for all frames "
+                         "(one kvp_session_run_frames_batched call); --matrix 2 runs both loops "
+                         "without it")
     ap.add_argument("--streaming", action="store_true",
                     help="with --matrix 3 or 5: streaming arena (sticky slots, LIFO reuse) instead of "
                          "re-staging every admitted row every frame")

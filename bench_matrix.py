@@ -56,8 +56,9 @@ def run_config5(*, reps: int = 3, frames: int = 16, tokens: int = 1560, heads: i
     frames (kvp.frames.run_frames_batched)."""
     loop = run_frames_batched if batched and not streaming else run_frames
     extra = {} if loop is run_frames_batched else {"streaming": streaming}
-    # timed passes run the loop natively (one kvp_session_run_frames call)
-    timed_extra = extra if loop is run_frames_batched else {**extra, "native": True}
+    # timed passes run the loop natively (one kvp_session_run_frames or
+    # kvp_session_run_frames_batched call)
+    timed_extra = {**extra, "native": True}
     from kvp._lib import DeviceInfo, lib
     import ctypes as C
     if max_persist is None:
@@ -133,7 +134,7 @@ def run_config2(*, reps: int = 3, frames: int = 8, tokens: int = 1560, heads: in
     for _ in range(reps):
         loop(q, k, v, out, scores, policy="recency", set_aside=set_aside, frames=frames,
              tokens=tokens, heads=heads, stream=stream, events=(e0, e1),
-             **({} if batched else {"native": True}))
+             native=True)
         ts.append(e0.elapsed_time(e1))
     t = float(np.mean(ts))
     return {"config": 2, "policy": "recency", "tiles": tiles, "frames": frames,

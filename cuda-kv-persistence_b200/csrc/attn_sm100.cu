@@ -141,7 +141,7 @@ __device__ __forceinline__ SegHot seg_hot(const Seg& g) {
 
 // Segments per launch: 1 for kvp_attn_bf16, up to kMaxSegs for
 // kvp_attn_bf16_multi (the table is a kernel parameter, 2.3 KB a segment).
-constexpr int kMaxSegs = 12;
+constexpr int kMaxSegs = kAttnSegsPerLaunch;
 
 template <int kSegs>
 struct SegTable {
@@ -1066,8 +1066,26 @@ int check_attn_bf16(const LayerIO& io, const AttnDesc& d) {
 namespace {
 
 // Tensor maps and pointers of one layer (check_attn_bf16 has passed).
-int fill_seg(Seg& g, const LayerIO& io, const AttnDesc& d) {
+// Whether two layers' segments would hold the same tensor maps.
+bool same_tensors(const LayerIO& a, const AttnDesc& da, const LayerIO& b, const AttnDesc& db) {
+    return a.q == b.q && a.k == b.k && a.v == b.v && a.arena == b.arena && a.q_rows == b.q_rows &&
+           a.kv_rows == b.kv_rows && (a.arena ? a.arena_rows == b.arena_rows : true) && da.heads == db.heads;
+}
+
+// like: a segment filled from a layer with the same tensors (same_tensors),
+// whose maps are copied instead of encoded again.
+int fill_seg(Seg& g, const LayerIO& io, const AttnDesc& d, const Seg* like = nullptr) {
     const int D = d.heads * kDH;
+    if (like) {
+        g = *like;
+        g.kvmap = io.kvmap;
+        g.out = (__nv_bfloat16*)io.out;
+        g.head0 = d.head0;
+        g.nheads = d.nheads;
+        g.cta0 = 0;
+        g.q_frame0 = d.q_frame0;
+        return KVP_OK;
+    }
     std::memset(&g, 0, sizeof g);
     // Box kinds whose height fits the tensor (a box never starts past the
     // end, and a taller box than the tensor is never encoded).
@@ -1259,7 +1277,9 @@ int launch_attn_bf16_multi(const LayerIO* ios, const AttnDesc* ds, int n, int* d
         const int cnt = n - first < per_launch ? n - first : per_launch;
         long long cta = 0;
         for (int i = 0; i < cnt; ++i) {
-            const int rc = fill_seg(tab.seg[i], ios[first + i], ds[first + i]);
+            const int k = first + i;
+            const bool like = i > 0 && same_tensors(ios[k], ds[k], ios[k - 1], ds[k - 1]);
+            const int rc = fill_seg(tab.seg[i], ios[k], ds[k], like ? &tab.seg[i - 1] : nullptr);
             if (rc) return rc;
             tab.seg[i].cta0 = (int)cta;
             cta += (long long)ds[first + i].nheads * P.items_per_head;

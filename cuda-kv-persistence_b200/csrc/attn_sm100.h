@@ -59,6 +59,9 @@ int launch_attn_bf16(const LayerIO& io, const AttnDesc& d, int* d_status, cudaSt
 // short chunk overlaps the next chunk's work; no key-range split.
 int launch_attn_bf16_multi(const LayerIO* ios, const AttnDesc* ds, int n, int* d_status,
                            cudaStream_t stream);
+// Layers one launch of launch_attn_bf16_multi takes (more are spread evenly
+// over several launches).
+constexpr int kAttnSegsPerLaunch = 12;
 
 // The launcher's argument checks alone (descriptor, row coverage, 16-byte
 // alignment), touching no device state: KVP_OK or KVP_ERR_ARG with a message.

@@ -1,6 +1,7 @@
 // extern "C" boundary of libkvp.so.  Declarations and the reference
 // interface each export replaces are in include/kv_tile_manager.h,
 // include/attn_kernel.h and include/kvp.h.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -636,6 +637,90 @@ KVP_API int kvp_session_run_frames(void* sp, int f0, int nframes, const float* s
         if (rc != kvp::KVP_OK) return rc;
         A.q_frame0 = f;
         rc = kvp::launch_attn_bf16(L, A, status, st);
+        if (rc != kvp::KVP_OK) return rc;
+    }
+    return persist ? s->clear_window(st) : kvp::KVP_OK;
+}
+
+// The dense-arena per-frame loop with every frame's attention in one grid
+// (kvp.h): admission needs nothing from the device, so all frames are
+// planned first, frame i staged into arena i with its own KVMap slice.
+KVP_API int kvp_session_run_frames_batched(void* sp, int f0, int nframes, const float* scores_flat,
+                                           const kvp_layer_io* io, const kvp_attn_desc* d,
+                                           long long* maps, void* stream) {
+    auto* s = static_cast<kvp::Session*>(sp);
+    if (!s || !io || !d || nframes <= 0 || f0 < 0) return kvp::KVP_ERR_ARG;
+    const kvp::SessionConfig& c = s->config();
+    const bool persist = s->persists();
+    if (c.mode != kvp::MODE_INTRA && c.mode != kvp::MODE_CROSS) {
+        kvp::set_error("run_frames_batched: needs an intra or cross session");
+        return kvp::KVP_ERR_ARG;
+    }
+    if (f0 + nframes > c.frames) {
+        kvp::set_error("run_frames_batched: frames [%d, %d) past the session's %d", f0, f0 + nframes,
+                       c.frames);
+        return kvp::KVP_ERR_ARG;
+    }
+    if (persist && (c.streaming || c.layers < nframes || !maps)) {
+        kvp::set_error("run_frames_batched: needs dense arenas (streaming 0), one per frame "
+                       "(layers %d < %d frames), and a device map buffer", c.layers, nframes);
+        return kvp::KVP_ERR_ARG;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t map_len = s->map_len();
+    // With the arenas back to back, every frame's map indexes them as one
+    // arena from arena(0) (kvp::Session::stage_batched): all segments then
+    // share their tensors, and one gather per chunk stages its frames.
+    const int64_t stride = persist ? s->arena_stride_rows() : 0;
+    // Frames go in chunks of at most one launch's segments, in frame order:
+    // a chunk is planned, staged and launched, and the device runs it while
+    // the host plans the next.  Within a chunk the longest key span comes
+    // first: entry c0 + j of chunk [c0, c0 + cnt) is frame c0 + cnt - 1 - j.
+    const int chunks = (nframes + kvp::kAttnSegsPerLaunch - 1) / kvp::kAttnSegsPerLaunch;
+    const int per = (nframes + chunks - 1) / chunks;
+    std::vector<kvp::LayerIO> L((size_t)nframes);
+    std::vector<kvp::AttnDesc> A((size_t)nframes);
+    for (int c0 = 0; c0 < nframes; c0 += per) {
+        const int cnt = std::min(per, nframes - c0);
+        for (int j = 0; j < cnt; ++j) {
+            const int fi = c0 + cnt - 1 - j;   // frame index within the call
+            kvp::LayerIO& l = L[(size_t)(c0 + j)];
+            l = kvp::LayerIO{io->q, io->k, io->v, io->out, nullptr, nullptr, io->q_rows, io->kv_rows, 0};
+            if (persist) {
+                l.kvmap = reinterpret_cast<const long long*>(maps + (size_t)fi * (size_t)map_len);
+                l.arena = s->arena(stride > 0 ? 0 : fi);
+                l.arena_rows = stride > 0 ? (long long)nframes * stride : s->cap_rows();
+            }
+            kvp::AttnDesc& a = A[(size_t)(c0 + j)];
+            a = kvp::AttnDesc{d->tokens, 1, f0 + fi, d->mode, d->window, d->heads, d->head_dim,
+                              d->head0, d->nheads, 0};
+            const int rc = kvp::check_attn_bf16(l, a);
+            if (rc != kvp::KVP_OK) return rc;
+        }
+    }
+    // Bad arguments are reported above, before any device work.
+    int* status = kvp::status_word();
+    if (!status) return kvp::KVP_ERR_CUDA;
+    int rc = kvp::KVP_OK;
+    for (int c0 = 0; c0 < nframes; c0 += per) {
+        const int cnt = std::min(per, nframes - c0);
+        if (stride > 0) {
+            rc = s->stage_batched(f0 + c0, cnt, c0, scores_flat, io->k, io->v,
+                                  reinterpret_cast<int64_t*>(maps), st);
+            if (rc != kvp::KVP_OK) return rc;
+        } else {
+            for (int i = c0; i < c0 + cnt; ++i) {
+                rc = s->plan_frame(f0 + i, scores_flat);
+                if (rc != kvp::KVP_OK) return rc;
+                if (!persist) continue;
+                if ((rc = s->upload_to(reinterpret_cast<int64_t*>(maps) + (size_t)i * (size_t)map_len, st)) !=
+                    kvp::KVP_OK)
+                    return rc;
+                if ((rc = s->stage_layer(i, io->k, io->v, st)) != kvp::KVP_OK) return rc;
+            }
+        }
+        if (persist && (rc = s->apply_window(c0 + cnt - 1, st)) != kvp::KVP_OK) return rc;
+        rc = kvp::launch_attn_bf16_multi(L.data() + c0, A.data() + c0, cnt, status, st);
         if (rc != kvp::KVP_OK) return rc;
     }
     return persist ? s->clear_window(st) : kvp::KVP_OK;

@@ -177,6 +177,19 @@ bool KVTileManager::arena_reserve(size_t total, long* out_row) {
     return true;
 }
 
+size_t KVTileManager::arena_reserve_rows(size_t total, size_t n, long* first_row) {
+    // arena_reserve n times: each row passes while the bytes used stay within
+    // both the budget and the capacity.
+    *first_row = (long)arena_next_row_;
+    const size_t lim = budget_bytes_ < arena_cap_ ? budget_bytes_ : arena_cap_;
+    if (total == 0 || arena_used_ >= lim) return total == 0 ? n : 0;
+    size_t k = (lim - arena_used_) / total;
+    if (k > n) k = n;
+    arena_next_row_ += k;
+    arena_used_ += k * total;
+    return k;
+}
+
 bool KVTileManager::arena_stage(const void* k_dev, size_t k_bytes, const void* v_dev,
                                 size_t v_bytes, long* out_row) {
     long row = -1;

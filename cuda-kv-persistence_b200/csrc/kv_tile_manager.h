@@ -95,6 +95,10 @@ public:
     // session's multi-layer gather kernel).  Same results as the staging
     // calls above; *copy_needed tells whether the row's data must be written.
     bool arena_reserve(size_t row_bytes_kv, long* out_row);
+    // arena_reserve for up to n rows in order, stopping at the first one it
+    // would refuse: returns how many it reserved, as rows *first_row ..
+    // *first_row + count - 1.
+    size_t arena_reserve_rows(size_t row_bytes_kv, size_t n, long* first_row);
     // *was_held (optional) tells whether row_id held a slot before the call.
     bool streaming_reserve(long row_id, size_t row_bytes_kv, bool changed, long* out_slot,
                            bool* copy_needed, bool* was_held = nullptr);

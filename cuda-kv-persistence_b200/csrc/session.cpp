@@ -86,23 +86,33 @@ int Session::stage_rows_of(int64_t gid, int64_t src_f, int64_t tile) {
     (void)gid;
     const int64_t t0 = layout_.tile_start(tile);
     const int64_t cnt = layout_.tile_count(tile);
+    if (!c_.streaming) {
+        // dense arena: consecutive slots, every row a copy
+        long first = -1;
+        const int64_t k = (int64_t)mgr_->arena_reserve_rows((size_t)(2 * row_kv_bytes_), (size_t)cnt, &first);
+        const int64_t row0 = src_f * c_.tokens + t0;
+        const size_t p0 = pairs_.size();
+        pairs_.resize(p0 + 2 * (size_t)k);
+        for (int64_t r = 0; r < k; ++r) {
+            map_[(size_t)(row0 + r)] = first + r;
+            pairs_[p0 + 2 * (size_t)r] = (int32_t)(row0 + r);
+            pairs_[p0 + 2 * (size_t)r + 1] = (int32_t)(first + r);
+        }
+        return k == cnt ? 1 : 0;
+    }
+    // streaming: a held row is a sticky hit, mapped without a copy
     bool all = true;
     for (int64_t r = 0; r < cnt && all; ++r) {
         const int64_t row_id = src_f * c_.tokens + t0 + r;
         long slot = -1;
         bool copy = false;
-        if (c_.streaming) {
-            all = mgr_->streaming_reserve((long)row_id, (size_t)(2 * row_kv_bytes_), false, &slot, &copy);
-        } else {
-            all = mgr_->arena_reserve((size_t)(2 * row_kv_bytes_), &slot);
-            copy = all;
-        }
+        all = mgr_->streaming_reserve((long)row_id, (size_t)(2 * row_kv_bytes_), false, &slot, &copy);
         if (all) {
             map_[(size_t)row_id] = slot;
             if (copy) {
                 pairs_.push_back((int32_t)row_id);
                 pairs_.push_back((int32_t)slot);
-            } else if (c_.streaming) {
+            } else {
                 ++info_.hits;
             }
         }
@@ -357,8 +367,10 @@ int Session::finish() {
     return KVP_OK;
 }
 
-int Session::upload(cudaStream_t s) {
-    if (!d_map_) return KVP_ERR_ARG;
+int Session::upload(cudaStream_t s) { return upload_to(d_map_, s); }
+
+int Session::upload_to(int64_t* dmap, cudaStream_t s, int64_t slot_offset) {
+    if (!d_map_ || !dmap) return KVP_ERR_ARG;
     const int64_t r0 = info_.map_row0, n = info_.map_rows;
     if (r0 < 0 || n < 0 || r0 + n > (int64_t)map_.size()) return KVP_ERR_ARG;
     // This slot's pinned buffers may still feed the upload made
@@ -366,11 +378,23 @@ int Session::upload(cudaStream_t s) {
     const int k = upload_slot_;
     upload_slot_ = (upload_slot_ + 1) % kUploadSlots;
     KVP_CUDA(cudaEventSynchronize(upload_done_[k]));
-    std::memcpy(h_map_pinned_[k] + r0, map_.data() + r0, (size_t)n * sizeof(int64_t));
-    KVP_CUDA(cudaMemcpyAsync(d_map_ + r0, h_map_pinned_[k] + r0, (size_t)n * sizeof(int64_t),
+    if (slot_offset == 0) {
+        std::memcpy(h_map_pinned_[k] + r0, map_.data() + r0, (size_t)n * sizeof(int64_t));
+    } else {
+        for (int64_t r = r0; r < r0 + n; ++r)
+            h_map_pinned_[k][r] = map_[(size_t)r] >= 0 ? map_[(size_t)r] + slot_offset : map_[(size_t)r];
+    }
+    KVP_CUDA(cudaMemcpyAsync(dmap + r0, h_map_pinned_[k] + r0, (size_t)n * sizeof(int64_t),
                              cudaMemcpyHostToDevice, s));
     if (!pairs_.empty()) {
-        std::memcpy(h_pairs_pinned_[k], pairs_.data(), pairs_.size() * sizeof(int32_t));
+        if (slot_offset == 0) {
+            std::memcpy(h_pairs_pinned_[k], pairs_.data(), pairs_.size() * sizeof(int32_t));
+        } else {
+            for (size_t p = 0; p < pairs_.size(); p += 2) {
+                h_pairs_pinned_[k][p] = pairs_[p];
+                h_pairs_pinned_[k][p + 1] = pairs_[p + 1] + (int32_t)slot_offset;
+            }
+        }
         KVP_CUDA(cudaMemcpyAsync(d_pairs_, h_pairs_pinned_[k], pairs_.size() * sizeof(int32_t),
                                  cudaMemcpyHostToDevice, s));
     }
@@ -422,6 +446,36 @@ int Session::produce(int layer, const void* x, const void* w, const float* bias,
     io.arena_rows = cap_rows_;
     io.D = c_.hidden;
     return launch_qkv_project_bf16(io, st, s);
+}
+
+int64_t Session::arena_stride_rows() const {
+    const int64_t row = 2 * row_kv_bytes_;
+    return (row > 0 && arena_layer_bytes_ > 0 && arena_layer_bytes_ % row == 0) ? arena_layer_bytes_ / row
+                                                                               : 0;
+}
+
+int Session::stage_batched(int f0, int n, int arena0, const float* scores_flat, const void* k,
+                           const void* v, int64_t* maps, cudaStream_t s) {
+    const int64_t stride = arena_stride_rows();
+    if (status_ != KVP_OK) return status_;
+    if (c_.streaming || (c_.mode != MODE_INTRA && c_.mode != MODE_CROSS) || c_.policy == POLICY_NONE ||
+        n <= 0 || arena0 < 0 || arena0 + n > c_.layers || stride <= 0 || !maps || !k || !v || !d_arena_) {
+        set_error("session stage_batched: needs a dense intra/cross session with a policy, one "
+                  "back-to-back arena per frame (%d frames, %d layers) and device buffers", n, c_.layers);
+        return KVP_ERR_ARG;
+    }
+    // Per frame: plan, upload its map slice and copy list with the slots
+    // moved to its arena (through the pinned ring), gather its rows.
+    const int64_t map_len = (int64_t)map_.size();
+    for (int i = 0; i < n; ++i) {
+        int rc = plan_frame(f0 + i, scores_flat);
+        if (rc != KVP_OK) return rc;
+        const int64_t off = (int64_t)(arena0 + i) * stride;
+        if (off + stride > INT32_MAX) return KVP_ERR_ARG;
+        if ((rc = upload_to(maps + (size_t)(arena0 + i) * (size_t)map_len, s, off)) != KVP_OK) return rc;
+        if ((rc = stage_layer(0, k, v, s)) != KVP_OK) return rc;
+    }
+    return KVP_OK;
 }
 
 int Session::stage_layer(int layer, const void* k, const void* v, cudaStream_t s) {

@@ -94,6 +94,25 @@ public:
     int64_t arena_layer_bytes() const { return arena_layer_bytes_; }
     // Uploads this step's map slice and copy list (pinned staging, async).
     int upload(cudaStream_t s);
+    // The same with the map slice going to `dmap` (device, map_len() entries,
+    // only this step's slice written) instead of the session's own map, and
+    // slot_offset added to every slot in the map and the copy list.
+    int upload_to(int64_t* dmap, cudaStream_t s, int64_t slot_offset = 0);
+    const SessionConfig& config() const { return c_; }
+    // Rows from one layer's arena to the next when the arenas sit back to
+    // back a whole number of rows apart (every layer's rows then index one
+    // arena of layers * stride rows from arena(0)), else 0.
+    int64_t arena_stride_rows() const;
+    // Dense-arena batch (not streaming, intra or cross, policy not None,
+    // arena0 + n <= layers, arena_stride_rows() > 0): frames f0 .. f0+n-1
+    // planned in order; frame f0 + i goes to arena a = arena0 + i: its KVMap
+    // slice is written (on `s`) to maps + a * map_len() with its slots moved
+    // to that arena (slot + a * stride: entries index the back-to-back
+    // arenas from arena(0)) and its rows are gathered there.  Entries outside
+    // each frame's slice are not written.  info() then describes the last
+    // frame.
+    int stage_batched(int f0, int n, int arena0, const float* scores_flat, const void* k,
+                      const void* v, int64_t* maps, cudaStream_t s);
     // Gathers this step's rows into every layer's arena, except source rows
     // in [skip_row0, skip_row0 + skip_rows) (rows a produce() call wrote).
     int stage(const void* const* k_layers, const void* const* v_layers, cudaStream_t s,

@@ -128,6 +128,9 @@ SIGNATURES = {
     "kvp_attn_bf16_multi": (C.c_int, [C.POINTER(LayerIO), C.POINTER(AttnDesc), C.c_int, C.c_void_p]),
     "kvp_session_run_frames": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                          C.POINTER(LayerIO), C.POINTER(AttnDesc), C.c_void_p]),
+    "kvp_session_run_frames_batched": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                                 C.POINTER(LayerIO), C.POINTER(AttnDesc),
+                                                 C.c_void_p, C.c_void_p]),
     "kvp_attn_bf16_noalloc": (C.c_int, [C.POINTER(LayerIO), C.POINTER(AttnDesc), C.c_void_p,
                                         C.POINTER(C.c_int), C.c_void_p]),
     "kvp_session_create": (C.c_void_p, [C.POINTER(SessionConfig)]),

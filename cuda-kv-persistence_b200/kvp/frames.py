@@ -117,12 +117,14 @@ def run_reuse_frames(q, k, v, out, scores, reuse, *, policy: str, set_aside: int
 
 def run_frames_batched(q, k, v, out, scores, *, policy: str, set_aside: int, frames: int,
                        tokens: int, heads: int, stream: int, events=None, mode: str = "cross",
-                       window: int = 0) -> dict:
+                       window: int = 0, native: bool = False) -> dict:
     """Arena-mode per-frame admission (the reference driver's default,
     src/run_policy_experiment.cu:189-256) with one attention grid for all
     frames.  Frame f's admission is planned as in run_frames and staged into
     arena f; its KVMap slice is kept in a device buffer of its own.  One
-    persisting window over frame F-1's arena covers the launch."""
+    persisting window over frame F-1's arena covers the launch.  native: the
+    whole pass in one kvp_session_run_frames_batched call (the per-frame
+    counters then come back as None)."""
     hidden = heads * 128
     amode = "causal" if mode == "cross" else "intra"
     win = window if mode == "cross" else 0
@@ -138,6 +140,14 @@ def run_frames_batched(q, k, v, out, scores, *, policy: str, set_aside: int, fra
     try:
         if events:
             events[0].record()
+        if native:
+            s.run_frames_batched(0, frames, scores, q, k, v, out, maps if persist else None,
+                                 heads=heads, mode=amode, window=win, stream=stream)
+            if events:
+                events[1].record()
+            torch.cuda.synchronize()
+            s.finish()
+            return {"copies": None, "staged_bytes": None}
         for f in range(frames):
             st = s.plan_frame(f, scores)
             copies += st.copies

@@ -163,6 +163,26 @@ class Session:
                                              None if r is None else r.ctypes.data, C.byref(io),
                                              C.byref(d), C.c_void_p(stream)), "run_frames")
 
+    def run_frames_batched(self, f0: int, nframes: int, scores_flat: np.ndarray, q, k, v, out,
+                           maps, *, heads: int, mode: str = "causal", window: int = 0,
+                           stream: int = 0):
+        """The dense-arena per-frame loop with all frames' attention in one
+        grid, in one native call (kvp_session_run_frames_batched): frame
+        f0 + i planned, its KVMap slice uploaded into maps[i] and its rows
+        staged into arena i; then one kvp_attn_bf16_multi over the frames.
+        maps: device int64 [nframes, frames * tokens] (None for the None
+        policy)."""
+        from ._lib import AttnDesc, LayerIO
+        sflat = np.ascontiguousarray(scores_flat, dtype=np.float32).reshape(-1)
+        io = LayerIO(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), 0, 0, q.shape[0],
+                     k.shape[0], 0)
+        d = AttnDesc(self.tokens, 1, f0, {"intra": 0, "causal": 1}[mode], window, heads, 128, 0,
+                     heads, 0)
+        mp = None if maps is None else C.c_void_p(maps.data_ptr())
+        check(self._L.kvp_session_run_frames_batched(self.h, f0, nframes, sflat.ctypes.data,
+                                                     C.byref(io), C.byref(d), mp,
+                                                     C.c_void_p(stream)), "run_frames_batched")
+
     def stage_except(self, k_ptrs, v_ptrs, skip_row0: int, skip_rows: int, stream: int = 0):
         """stage() without the source rows [skip_row0, skip_row0 + skip_rows)."""
         n = len(k_ptrs)

@@ -273,6 +273,26 @@ int kvp_session_step(void* s, int frame, const float* scores_flat, const signed 
 int kvp_session_run_frames(void* s, int f0, int nframes, const float* scores_flat,
                            const signed char* reuse_flat, const kvp_layer_io* io,
                            const kvp_attn_desc* d, void* stream);
+/* The same loop for a dense-arena session (streaming 0, intra or cross) with
+ * the frames' attention merged into one grid (no reference counterpart:
+ * admission reads only the motion scores, so frames can be planned before
+ * any runs).  The frames go in chunks of up to 12 (16 frames: 8 + 8), in
+ * frame order.  For each frame f0 + i of a chunk: kvp_session_plan_frame,
+ * then, unless the policy is None, its KVMap slice is uploaded into
+ * maps + i * (frames * tokens) and its admitted rows are staged into arena
+ * i.  Then a persisting window over the chunk's last arena and one
+ * kvp_attn_bf16_multi launch over the chunk (longest key span first); the
+ * host plans the next chunk while the device runs this one.  Finally the
+ * window is cleared.  Each frame reads the rows it reads in
+ * kvp_session_run_frames, so the outputs are the same bytes.
+ * Needs a session with layers >= nframes and, unless the policy is None,
+ * `maps`: a device int64 buffer of nframes * frames * tokens entries owned
+ * by the caller (only each frame's slice is written).  io->arena /
+ * io->kvmap / io->arena_rows are ignored.  Bad arguments are reported before
+ * any device work. */
+int kvp_session_run_frames_batched(void* s, int f0, int nframes, const float* scores_flat,
+                                   const kvp_layer_io* io, const kvp_attn_desc* d,
+                                   long long* maps, void* stream);
 
 #ifdef __cplusplus
 }

@@ -223,3 +223,45 @@ def test_session_run_frames_rejects_bad_arguments():
         assert f(s.h, 0, 2, scores.ctypes.data, None, C.byref(io), C.byref(d64), None) == ERR_ARG
     finally:
         s.close()
+
+
+def test_session_run_frames_batched_rejects_bad_arguments():
+    """kvp_session_run_frames_batched refuses a missing session, descriptor or
+    frame range, a session it cannot batch (stack mode, streaming slots,
+    fewer arenas than frames, no map buffer) and a bad descriptor, all before
+    any device work."""
+    from kvp.session import Session
+    io = LayerIO(0x10000, 0x20000, 0x30000, 0x40000, 0, 0, 600, 600, 0)
+    d = AttnDesc(300, 1, 0, 1, 0, 2, 128, 0, 2, 0)
+    scores = np.zeros(3 * 19, dtype=np.float32)
+    f = lib().kvp_session_run_frames_batched
+    maps = C.c_void_p(0x50000)
+
+    def call(s, f0, n, io_=C.byref(io), d_=C.byref(d), m=maps):
+        return f(s, f0, n, scores.ctypes.data, io_, d_, m, None)
+
+    s = Session(mode="cross", policy="none", frames=3, tokens=300, hidden=256, elem_bytes=2,
+                set_aside=0, layers=0)
+    try:
+        assert call(None, 0, 2) == ERR_ARG
+        assert call(s.h, 0, 0) == ERR_ARG
+        assert call(s.h, -1, 2) == ERR_ARG
+        assert call(s.h, 0, 2, io_=None) == ERR_ARG
+        assert call(s.h, 0, 2, d_=None) == ERR_ARG
+        assert call(s.h, 2, 2) == ERR_ARG                      # frames 2, 3 of a 3-frame session
+        assert b"past the session" in lib().kvp_last_error()
+        # 3 frames of 300 rows do not fit the 600 rows the buffers hold
+        assert call(s.h, 0, 3) == ERR_ARG
+        d64 = AttnDesc(300, 1, 0, 1, 0, 2, 64, 0, 2, 0)
+        assert call(s.h, 0, 2, d_=C.byref(d64)) == ERR_ARG
+    finally:
+        s.close()
+    for kw, what in ((dict(mode="cross", policy="recency", layers=0), b"one per frame"),
+                     (dict(mode="cross", policy="recency", layers=0, streaming=True), b"streaming 0"),
+                     (dict(mode="stack", policy="recency", layers=0), b"intra or cross")):
+        s = Session(frames=3, tokens=300, hidden=256, elem_bytes=2, set_aside=1 << 20, **kw)
+        try:
+            assert call(s.h, 0, 2) == ERR_ARG, kw
+            assert what in lib().kvp_last_error(), (kw, lib().kvp_last_error())
+        finally:
+            s.close()

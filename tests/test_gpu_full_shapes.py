@@ -119,9 +119,10 @@ def test_config5_full_budget(inputs16, oracle16, regime, streaming):
 @pytest.mark.parametrize("config", ["2", "5-high"])
 def test_batched_frames_match_the_per_frame_loop(inputs16, oracle16, monkeypatch, config):
     """Arena mode with every frame planned first, staged into an arena of its
-    own and run in one grid (kvp.frames.run_frames_batched): each policy's
-    output is bitwise the per-frame loop's (key split off, which the batched
-    grid never uses), bitwise None's, and within the bf16 gates."""
+    own and run in one grid (kvp.frames.run_frames_batched, step by step and
+    as one kvp_session_run_frames_batched call): each policy's output is
+    bitwise the per-frame loop's (key split off, which the batched grid never
+    uses), bitwise None's, and within the bf16 gates."""
     from kvp.attention import read_status
     from kvp.frames import run_frames, run_frames_batched
     monkeypatch.setenv("KVP_ATTN_SPLITS", "1")
@@ -138,11 +139,15 @@ def test_batched_frames_match_the_per_frame_loop(inputs16, oracle16, monkeypatch
     for policy in policies:
         a = torch.full_like(q, float("nan"))
         b = torch.full_like(q, float("nan"))
+        c = torch.full_like(q, float("nan"))
         run_frames_batched(q, k, v, a, scores, policy=policy, set_aside=budget, frames=F, tokens=T,
                            heads=H, stream=stream)
         run_frames(q, k, v, b, scores, policy=policy, set_aside=budget, frames=F, tokens=T,
                    heads=H, stream=stream)
+        run_frames_batched(q, k, v, c, scores, policy=policy, set_aside=budget, frames=F, tokens=T,
+                           heads=H, stream=stream, native=True)
         assert torch.equal(a, b), policy
+        assert torch.equal(c, b), policy
         outs[policy] = a.float().cpu().numpy()
     assert read_status() == 0
     want = oracle16 if F == 16 else _oracle_heads(q, k, v, F)
