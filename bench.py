@@ -251,6 +251,7 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
     flat = [torch.empty(local_elems, dtype=torch.bfloat16, device=dev) for _ in range(2)]
     gathered = (torch.empty(local_elems * world, dtype=torch.bfloat16, device=dev)
                 if world > 1 else None)
+    ce = CopyEngineGather(gathered, flat, rank, world, dev) if world > 1 and args.gather == "ce" else None
 
     def bind_outputs(buf):
         off = 0
@@ -300,12 +301,15 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
         if world > 1:
             ev = torch.cuda.Event()
             ev.record(stream)
-            comm.wait_event(ev)
-            with torch.cuda.stream(comm):
-                dist.all_gather_into_tensor(gathered, flat[b])
-            done = torch.cuda.Event()
-            done.record(comm)
-            gather_done[b] = done
+            if ce is not None:
+                gather_done[b] = ce.push(b, ev)
+            else:
+                comm.wait_event(ev)
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(gathered, flat[b])
+                done = torch.cuda.Event()
+                done.record(comm)
+                gather_done[b] = done
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -326,6 +330,8 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
         one_step(args.warmup + i, True)
     if world > 1:
         stream.wait_stream(comm)
+        if ce is not None:
+            ce.join(stream)
     t1.record(stream)
     barrier()
     clocks = sampler.stop() if sampler else None
@@ -400,7 +406,9 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
                        "mask": "block-causal by frame",
                        "flop_per_step": total_flops,
                        "l2": "inputs 12.1 GB exceed the 126 MB L2 (no flush needed)",
-                       "parallelism": f"pairs/{world}" + (" + nccl all_gather" if world > 1 else "")},
+                       "parallelism": f"pairs/{world}" + ((" + nccl all_gather" if ce is None else
+                                                           " + copy-engine all_gather (peer copies)")
+                                                          if world > 1 else "")},
             "roofline": roofline,
             "dram": profiled_dram_per_step(),
             "cpu_baseline": cpu,
@@ -414,9 +422,84 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
         if status != 0:
             result = 3
     if world > 1:
+        torch.cuda.synchronize(dev)
         dist.barrier(device_ids=[local_rank])
+        if ce is not None:
+            ce.close()
+            dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
     return result
+
+
+class CopyEngineGather:
+    """The outputs' all-gather done by the copy engines instead of NCCL's
+    kernels: each rank writes its segment straight into every peer's
+    gathered buffer (CUDA IPC, cudaMemcpyAsync over NVLink), one stream per
+    peer.  The attention grid fills every SM, and a collective's CTAs would
+    take SMs from it; copy engines take none."""
+
+    def __init__(self, gathered, flat, rank, world, dev):
+        import torch
+        import torch.distributed as dist
+        from cuda.bindings import driver as cu, runtime as rt
+        self.rt, self.rank, self.world = rt, rank, world
+        self.nbytes = flat[0].numel() * flat[0].element_size()
+        self.flat_ptr = [t.data_ptr() for t in flat]
+        ptr = gathered.data_ptr()
+        err, base, _ = cu.cuMemGetAddressRange(ptr)
+        self._check(err, "cuMemGetAddressRange")
+        err, handle = rt.cudaIpcGetMemHandle(int(base))
+        self._check(err, "cudaIpcGetMemHandle")
+        objs = [None] * world
+        dist.all_gather_object(objs, (bytes(handle.reserved), ptr - int(base)))
+        self.opened, self.dst = [], {}
+        for p in range(world):
+            if p == rank:
+                self.dst[p] = ptr + rank * self.nbytes
+                continue
+            h = rt.cudaIpcMemHandle_t()
+            h.reserved = objs[p][0]
+            err, pbase = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+            self._check(err, f"cudaIpcOpenMemHandle(rank {p})")
+            self.opened.append(int(pbase))
+            self.dst[p] = int(pbase) + objs[p][1] + rank * self.nbytes
+        self.streams = {p: torch.cuda.Stream(device=dev) for p in range(world)}
+        self.torch = torch
+
+    @staticmethod
+    def _check(err, what):
+        if int(err) != 0:
+            raise RuntimeError(f"{what} failed: {err}")
+
+    def push(self, b, ready):
+        """Copy output buffer b to every rank once `ready` has passed; returns
+        an event that passes once every copy has read the buffer."""
+        kind = self.rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice
+        dones = []
+        for p, st in self.streams.items():
+            st.wait_event(ready)
+            err, = self.rt.cudaMemcpyAsync(self.dst[p], self.flat_ptr[b], self.nbytes, kind,
+                                           self.rt.cudaStream_t(st.cuda_stream))
+            self._check(err, "cudaMemcpyAsync")
+            e = self.torch.cuda.Event()
+            e.record(st)
+            dones.append(e)
+        # one event on the first stream that follows every copy
+        head = self.streams[0]
+        for e in dones[1:]:
+            head.wait_event(e)
+        done = self.torch.cuda.Event()
+        done.record(head)
+        return done
+
+    def join(self, stream):
+        for st in self.streams.values():
+            stream.wait_stream(st)
+
+    def close(self):
+        for pb in self.opened:
+            self.rt.cudaIpcCloseMemHandle(pb)
+        self.opened = []
 
 
 def run_e2e(args, stack, scores, dev, stream, world, local_rank):
@@ -598,6 +681,9 @@ def main() -> int:
                          "per-frame streaming loop, so admitted rows of the current frame are "
                          "written by the QKV epilogue instead of staged")
     ap.add_argument("--reps", type=int, default=3, help="repetitions per cell with --matrix (ABBA)")
+    ap.add_argument("--gather", choices=["nccl", "ce"], default="nccl",
+                    help="with --gpus > 1: all-gather the outputs with NCCL, or with the copy engines "
+                         "(every rank writes its segment into each peer's buffer over CUDA IPC)")
     ap.add_argument("--regime", choices=["static", "high", "both"], default="both",
                     help="--matrix 11: motion regimes")
     ap.add_argument("--budgets", default="0.1,1.0",
