@@ -647,7 +647,51 @@ attn_bf16_sm100_kernel(const __grid_constant__ SegTable<kSegs> tab, const __grid
             // were seen ready then follows without a wait.  (A completed phase
             // stays completed until this thread's own later MMAs let it move.)
             bool k_known = false;              // K(j) seen landed
+            // Steps 1 .. jf-1 have all four GEMMs and no last-step commits:
+            // they run in a loop of their own, with nothing between two GEMMs
+            // but the barrier tests and waits they need.
+            const int jf = own_release ? 0 : (n0 - 1 < n1 ? n0 - 1 : n1);
             for (int j = 0; ok && j < n_tiles; ++j) {
+                if (j == 1 && jf > 1) {
+                    for (; j < jf; ++j) {
+                        if (!k_known && !mbar_wait(&sm.bar_kfull[ks], kph, sm, P.status)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint64_t kd = dk + ks * kStageDesc;
+                        tc_gemm_ss_head(s0_tm, dq0, kd, idS);
+                        const bool pv1_ready = mbar_test(&sm.bar_p_full[1], (uint32_t)(j - 1) & 1u);
+                        tc_gemm_ss_tail(s0_tm, dq0, kd, idS);
+                        tc_commit(&sm.bar_s_full[0]);
+                        if (!pv1_ready && !mbar_wait(&sm.bar_p_full[1], (uint32_t)(j - 1) & 1u, sm, P.status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t vd1 = dv + pvs * kStageDesc;
+                        tc_gemm_ts_head(o1_tm, s1_tm, vd1, idO, j > 1 ? 1u : 0u);
+                        tc_gemm_ts_tail(o1_tm, s1_tm, vd1, idO);
+                        tc_gemm_ss_head(s1_tm, dq1, kd, idS);
+                        const bool pv0_ready = mbar_test(&sm.bar_vfull[vs], vph) &&
+                                               mbar_test(&sm.bar_p_full[0], (uint32_t)j & 1u);
+                        tc_gemm_ss_tail(s1_tm, dq1, kd, idS);
+                        tc_commit(&sm.bar_s_full[1]);
+                        const uint32_t ks_n = ks + 1 == kKStages ? 0u : ks + 1;
+                        const uint32_t kph_n = ks + 1 == kKStages ? kph ^ 1u : kph;
+                        if (!pv0_ready && (!mbar_wait(&sm.bar_vfull[vs], vph, sm, P.status) ||
+                                           !mbar_wait(&sm.bar_p_full[0], (uint32_t)j & 1u, sm, P.status))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t vd0 = dv + vs * kStageDesc;
+                        tc_gemm_ts_head(o0_tm, s0_tm, vd0, idO, 1u);
+                        k_known = mbar_test(&sm.bar_kfull[ks_n], kph_n);
+                        tc_gemm_ts_tail(o0_tm, s0_tm, vd0, idO);
+                        pvs = vs; pvph = vph;
+                        if (++vs == kVStages) { vs = 0; vph ^= 1u; }
+                        ks = ks_n; kph = kph_n;
+                    }
+                    if (!ok || j >= n_tiles) break;
+                }
                 if (!k_known && !mbar_wait(&sm.bar_kfull[ks], kph, sm, P.status)) { ok = false; break; }
                 tc_fence_after();
                 const bool pv1 = j >= 1 && j - 1 < n1;
