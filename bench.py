@@ -253,6 +253,8 @@ def run_kvp(args, rank: int, world: int, local_rank: int) -> int:
     gathered = (torch.empty(local_elems * world, dtype=torch.bfloat16, device=dev)
                 if world > 1 else None)
     ce = CopyEngineGather(gathered, flat, rank, world, dev) if world > 1 and args.gather == "ce" else None
+    if ce is not None and not ce.ok:
+        ce = None   # every rank falls back to NCCL together
 
     def bind_outputs(buf):
         off = 0
@@ -443,29 +445,47 @@ class CopyEngineGather:
         import torch
         import torch.distributed as dist
         from cuda.bindings import driver as cu, runtime as rt
-        self.rt, self.rank, self.world = rt, rank, world
+        self.rt, self.rank, self.world, self.torch = rt, rank, world, torch
         self.nbytes = flat[0].numel() * flat[0].element_size()
         self.flat_ptr = [t.data_ptr() for t in flat]
-        ptr = gathered.data_ptr()
-        err, base, _ = cu.cuMemGetAddressRange(ptr)
-        self._check(err, "cuMemGetAddressRange")
-        err, handle = rt.cudaIpcGetMemHandle(int(base))
-        self._check(err, "cudaIpcGetMemHandle")
-        objs = [None] * world
-        dist.all_gather_object(objs, (bytes(handle.reserved), ptr - int(base)))
         self.opened, self.dst = [], {}
-        for p in range(world):
-            if p == rank:
-                self.dst[p] = ptr + rank * self.nbytes
-                continue
-            h = rt.cudaIpcMemHandle_t()
-            h.reserved = objs[p][0]
-            err, pbase = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
-            self._check(err, f"cudaIpcOpenMemHandle(rank {p})")
-            self.opened.append(int(pbase))
-            self.dst[p] = int(pbase) + objs[p][1] + rank * self.nbytes
-        self.streams = {p: torch.cuda.Stream(device=dev) for p in range(world)}
-        self.torch = torch
+        ptr = gathered.data_ptr()
+        # Every rank takes the same collective steps whatever fails locally:
+        # export, exchange, import, then agree; if any rank could not, none
+        # uses the copy engines (self.ok False: the caller falls back).
+        mine = None
+        try:
+            err, base, _ = cu.cuMemGetAddressRange(ptr)
+            self._check(err, "cuMemGetAddressRange")
+            err, handle = rt.cudaIpcGetMemHandle(int(base))
+            self._check(err, "cudaIpcGetMemHandle")
+            mine = (bytes(handle.reserved), ptr - int(base))
+        except Exception as e:  # noqa: BLE001 -- reported, then agreed on below
+            print(f"rank {rank}: copy-engine gather unavailable ({e})", flush=True)
+        objs = [None] * world
+        dist.all_gather_object(objs, mine)
+        ok = all(o is not None for o in objs)
+        if ok:
+            try:
+                for p in range(world):
+                    if p == rank:
+                        self.dst[p] = ptr + rank * self.nbytes
+                        continue
+                    h = rt.cudaIpcMemHandle_t()
+                    h.reserved = objs[p][0]
+                    err, pbase = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                    self._check(err, f"cudaIpcOpenMemHandle(rank {p})")
+                    self.opened.append(int(pbase))
+                    self.dst[p] = int(pbase) + objs[p][1] + rank * self.nbytes
+            except Exception as e:  # noqa: BLE001
+                print(f"rank {rank}: copy-engine gather unavailable ({e})", flush=True)
+                ok = False
+        flag = torch.tensor([1 if ok else 0], device=dev, dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        self.ok = bool(flag.item())
+        if not self.ok:
+            self.close()
+        self.streams = {p: torch.cuda.Stream(device=dev) for p in range(world)} if self.ok else {}
 
     @staticmethod
     def _check(err, what):

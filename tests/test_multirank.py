@@ -117,3 +117,30 @@ def test_dead_peer_is_detected_on_the_host(tmp_path):
         p.join(timeout=120)
         assert not p.is_alive()
     assert (tmp_path / "rank0").read_text().startswith("error")
+
+
+def _worker_ce_fallback(rank, world, port, out_dir):
+    _init(rank, world, port, timeout_s=30)
+    import bench
+    from cuda.bindings import driver as cu, runtime as rt
+    if rank == 0:
+        # rank 0 exports a (fake) handle; rank 1 fails (no GPU here)
+        class _H:
+            reserved = bytes(64)
+        cu.cuMemGetAddressRange = lambda ptr: (0, ptr, 1 << 20)
+        rt.cudaIpcGetMemHandle = lambda base: (0, _H())
+    flat = [torch.zeros(16, dtype=torch.bfloat16) for _ in range(2)]
+    gathered = torch.zeros(16 * world, dtype=torch.bfloat16)
+    ce = bench.CopyEngineGather(gathered, flat, rank, world, "cpu")
+    (Path(out_dir) / f"rank{rank}").write_text("ok" if ce.ok else "fallback")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_copy_engine_gather_falls_back_on_every_rank(tmp_path):
+    """bench.CopyEngineGather: when one rank cannot export or open its IPC
+    handle, every rank takes the same collective steps and all fall back to
+    NCCL together (none is left waiting in a collective the others skip)."""
+    mp.spawn(_worker_ce_fallback, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    assert (tmp_path / "rank0").read_text() == "fallback"
+    assert (tmp_path / "rank1").read_text() == "fallback"
