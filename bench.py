@@ -8,8 +8,8 @@ block-causal by frame.  The 360 (layer, head) pairs are split into
 contiguous blocks over the ranks (fixed total work: strong scaling); each
 rank runs its pairs through the remapped-attention path and the per-rank
 outputs are all-gathered over NVLink on separate streams, one step behind,
-so the transfer overlaps the next step's compute: by the copy engines
-(peer copies over CUDA IPC, the default) or by NCCL (`--gather nccl`).
+so the transfer overlaps the next step's compute: by NCCL (the default) or
+by the copy engines (peer copies over CUDA IPC, `--gather ce`).
 
 One step = one stack admission (ReuseWeighted over all 21*98 tiles, budget
 = this GPU's cudaDevAttrMaxPersistingL2CacheSize), KVMap upload, one
@@ -702,10 +702,11 @@ def main() -> int:
                          "per-frame streaming loop, so admitted rows of the current frame are "
                          "written by the QKV epilogue instead of staged")
     ap.add_argument("--reps", type=int, default=3, help="repetitions per cell with --matrix (ABBA)")
-    ap.add_argument("--gather", choices=["ce", "nccl"], default="ce",
-                    help="with --gpus > 1: all-gather the outputs with the copy engines (every rank "
-                         "writes its segment into each peer's buffer over CUDA IPC; no SMs taken "
-                         "from the attention), or with NCCL's all_gather_into_tensor")
+    ap.add_argument("--gather", choices=["nccl", "ce"], default="nccl",
+                    help="with --gpus > 1: all-gather the outputs with NCCL's all_gather_into_tensor "
+                         "(the north-star's exchange), or with the copy engines (every rank writes its "
+                         "segment into each peer's buffer over CUDA IPC; no SMs taken from the "
+                         "attention)")
     ap.add_argument("--regime", choices=["static", "high", "both"], default="both",
                     help="--matrix 11: motion regimes")
     ap.add_argument("--budgets", default="0.1,1.0",
