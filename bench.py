@@ -703,10 +703,9 @@ def main() -> int:
                          "written by the QKV epilogue instead of staged")
     ap.add_argument("--reps", type=int, default=3, help="repetitions per cell with --matrix (ABBA)")
     ap.add_argument("--gather", choices=["nccl", "ce"], default="nccl",
-                    help="with --gpus > 1: all-gather the outputs with NCCL's all_gather_into_tensor "
-                         "(the north-star's exchange), or with the copy engines (every rank writes its "
-                         "segment into each peer's buffer over CUDA IPC; no SMs taken from the "
-                         "attention)")
+                    help="with --gpus > 1: all-gather the outputs with NCCL's all_gather_into_tensor, "
+                         "or with the copy engines (every rank writes its segment into each peer's "
+                         "buffer over CUDA IPC; no SMs taken from the attention)")
     ap.add_argument("--regime", choices=["static", "high", "both"], default="both",
                     help="--matrix 11: motion regimes")
     ap.add_argument("--budgets", default="0.1,1.0",

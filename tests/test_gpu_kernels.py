@@ -7,7 +7,8 @@ KVMap (tests/test_policy_variants.py:174-176 of the reference).
 
 Tolerances: FP32 path max-abs < 1e-3 and mean-abs < 1e-4
 (tests/test_correctness.py:26-27); BF16 tcgen05 path max-abs < 2e-2 against
-the fp32 oracle on the same bf16-rounded inputs.
+the fp32 oracle on the same bf16-rounded inputs (the bf16 path's stated
+tolerance).
 """
 
 from __future__ import annotations
