@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kvp|reference]
 
-Workload: 21 latent frames x 1560 tokens = 32,760 tokens,
+Workload (benchmark config 4): 21 latent frames x 1560 tokens = 32,760 tokens,
 30 layers x 12 heads x 128 (hidden 1536), bf16, Q/K/V ~ N(0,1)/sqrt(128),
 block-causal by frame.  The 360 (layer, head) pairs are split into
 contiguous blocks over the ranks (fixed total work: strong scaling); each

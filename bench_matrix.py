@@ -1,4 +1,4 @@
-"""bench.py's per-frame measurements (`--matrix N`)
+"""bench.py's per-frame measurements (`--matrix N`): benchmark config 5
 (policy x budget x motion regime), config 2 (8-frame cross, Recency),
 config 3 (50-frame trace, 30 layers, 5-frame causal window,
 ReuseWeighted) and the extension legs (temporal reuse, QKV producer,
@@ -259,7 +259,7 @@ def run_reuse_matrix(*, reps: int = 3, frames: int = 16, tokens: int = 1560, hea
     previous frame's rows.  Legs: "none" (no map), "dense" (dense arena, every
     admitted row copied every frame, the reference's staging), "reuse"
     (Session mode reuse).  Every leg's output must equal None's bitwise.
-    Traces: AR(1) rho 0.9 (BASELINE config 2's motion model, temporally
+    Traces: AR(1) rho 0.9 (benchmark config 2's motion model, temporally
     coherent) and config 5 'high' (i.i.d. per frame); reuse flags by the
     percentile-50 rule."""
     from kvp._lib import DeviceInfo, lib
@@ -338,7 +338,7 @@ def run_reuse_matrix(*, reps: int = 3, frames: int = 16, tokens: int = 1560, hea
 def run_producer(*, reps: int = 20, warmup: int = 3, frames: int = 21, tokens: int = 1560,
                  heads: int = 12, seed: int = 0, set_aside: int | None = None,
                  device="cuda") -> list[dict]:
-    """One layer's K/V production for BASELINE config 4 (21 frames x 1560
+    """One layer's K/V production for benchmark config 4 (21 frames x 1560
     tokens, D = 1536, stack admission by ReuseWeighted at the device's max
     persisting L2), CUDA events over `reps` calls each:
       fused         LayerNorm + the tcgen05 producer, which writes every

@@ -129,7 +129,7 @@ def csv_round_trip(scores: np.ndarray, workdir) -> np.ndarray:
     return read_motion_csv(p, *np.asarray(scores).shape)
 
 
-# ---------------------------------------------------------------- BASELINE configs
+# ---------------------------------------------------------------- benchmark configs
 def motion_config1(seed: int = 0, tiles: int = 98) -> np.ndarray:
     """Config 1: one frame, U[0,1) per tile."""
     g = torch.Generator().manual_seed(seed)

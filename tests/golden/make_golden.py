@@ -10,7 +10,7 @@ where they exist; the tests only read the files it writes:
 * ``motion_*.csv``        motion traces: the reference's synthetic 8-frame
                           trace (seed 42, produced by importing the
                           reference's traces/gen_synthetic_motion.py) and the
-                          BASELINE config generators (kvp/traces.py).
+                          benchmark config generators (kvp/traces.py).
 * ``kvmap_ref.json``      per-frame SHA-256 (first 16 hex) of the KVMap slice
                           each kernel launch receives, plus the staged-byte
                           counters, from the reference's UNMODIFIED driver

@@ -8,7 +8,7 @@ oracle/_ref/policy_experiment_gpu is the reference's complete program,
 kernel included, built for sm_100a; oracle/_ref/policy_experiment_ref is the
 same driver built for the host with the reference's manager and policies.
 
-On BASELINE configs 1 (one 1560-token frame, MotionGated, 22 fp32 tiles) and
+On benchmark configs 1 (one 1560-token frame, MotionGated, 22 fp32 tiles) and
 2 (8 frames, causal cross-frame, Recency, 22 tiles; arena and streaming):
 
 * what the driver prints (slots, the frame-0 selection, the streamed

@@ -1,4 +1,4 @@
-"""BASELINE configs 2, 3 and 5 at their own shapes on the GPU.
+"""benchmark configs 2, 3 and 5 at their own shapes on the GPU.
 
 The reference gates its full configurations on bitwise equality of every
 policy's output with the None policy's (tests/test_policy_variants.py:174-179)
