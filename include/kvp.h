@@ -280,7 +280,11 @@ int kvp_session_run_frames(void* s, int f0, int nframes, const float* scores_fla
  * frame order.  For each frame f0 + i of a chunk: kvp_session_plan_frame,
  * then, unless the policy is None, its KVMap slice is uploaded into
  * maps + i * (frames * tokens) and its admitted rows are staged into arena
- * i.  Then a persisting window over the chunk's last arena and one
+ * i.  When the session's arenas sit back to back a whole number of rows
+ * apart (the usual case), frame i's map entries index them as one block from
+ * arena 0 (slot + i * that stride), so every frame of a launch shares one
+ * set of tensor maps; otherwise they are arena i's own slots.  Then a
+ * persisting window over the chunk's last arena and one
  * kvp_attn_bf16_multi launch over the chunk (longest key span first); the
  * host plans the next chunk while the device runs this one.  Finally the
  * window is cleared.  Each frame reads the rows it reads in
