@@ -173,3 +173,35 @@ def test_native_loop_matches_the_python_loop(inputs16, streaming):
         run_frames(q, k, v, b, scores, **kw)
         assert torch.equal(a, b), policy
     assert read_status() == 0
+
+
+@pytest.mark.parametrize("mode,window", [("cross", 5), ("intra", 0)], ids=["cross-window5", "intra"])
+def test_native_batched_loop_window_and_intra(inputs16, monkeypatch, mode, window):
+    """kvp_session_run_frames_batched with a 5-frame causal window (config 3's
+    shape, 6 frames, ReuseWeighted at the full budget) and in intra mode
+    (8 frames, Recency, 22 tiles): bitwise the per-frame loop (key split off,
+    which the batched grid never uses), and None's."""
+    from kvp.attention import read_status
+    from kvp.frames import run_frames, run_frames_batched
+    monkeypatch.setenv("KVP_ATTN_SPLITS", "1")
+    if mode == "cross":
+        F, budget, policies = 6, _max_persist(), ("none", "reuse_weighted")
+        scores = read_motion_csv(GOLDEN / "motion_config3.csv", 50, TILES)[:F]
+    else:
+        F, budget, policies = 8, 2162688, ("none", "recency")
+        scores = read_motion_csv(GOLDEN / "motion_config2.csv", 8, TILES)
+    q, k, v = (t[:F * T] for t in inputs16)
+    stream = int(torch.cuda.current_stream().cuda_stream)
+    read_status()
+    outs = {}
+    for policy in policies:
+        a = torch.full_like(q, float("nan"))
+        b = torch.full_like(q, float("nan"))
+        kw = dict(policy=policy, set_aside=budget, frames=F, tokens=T, heads=H, stream=stream,
+                  mode=mode, window=window)
+        run_frames_batched(q, k, v, a, scores, native=True, **kw)
+        run_frames(q, k, v, b, scores, **kw)
+        assert torch.equal(a, b), policy
+        outs[policy] = a
+    assert torch.equal(outs[policies[0]], outs[policies[1]])
+    assert read_status() == 0
